@@ -1,0 +1,425 @@
+#!/usr/bin/env python3
+"""Benchmark of the attention hot path on B200 (one process per GPU).
+
+Headline workload (BASELINE config #3): causal flash-attention-2 forward +
+backward, bf16, B=8, H=32, S=4096, D=128.  A step is one forward and one
+backward over this rank's share of the B*H heads (strong scaling: the 256
+heads are split across the N ranks with no collective on the data path).
+Also measured: RoPE + head transpose (config #2, [4,2048,32,128] bf16) GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Rank 0 prints one JSON line.  Timing: CUDA events on the launching stream,
+barrier + synchronize on both sides, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FA2 fwd/bwd TFLOP/s (bf16 causal S4096 D128) at 1/2/4/8 B200; RoPE GB/s"
+CFG3 = dict(batch=8, heads=32, seq=4096, head_dim=128, causal=True)
+CFG2 = dict(batch=4, seq=2048, heads=32, head_dim=128, rope_base=10000.0)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def attn_flops(B, H, S, D, causal=True):
+    """FA2 convention: fwd 4*B*H*S^2*D (x1/2 causal), bwd = 2.5 x fwd."""
+    fwd = 4.0 * B * H * S * S * D * (0.5 if causal else 1.0)
+    return fwd, 2.5 * fwd
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in self.gpus:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() in ("active", "1"):
+                        reasons.add(n)
+        finally:
+            os.unlink(self.path)
+        if not sm:
+            return None
+        top = max(sm)
+        loaded = [s for s in sm if s >= 0.5 * top] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU legs
+def cpu_attention_sample(threads=None):
+    """Oracle (fp32 restatement of the reference kernels) on one (b,h) slice
+    of config #3 at full S: causal fwd + bwd.  Returns (seconds, flops)."""
+    import numpy as np
+    import oracle
+
+    if threads:
+        oracle.set_threads(threads)
+    S, D = CFG3["seq"], CFG3["head_dim"]
+    rng = np.random.default_rng(42)
+    q, k, v, do = (rng.standard_normal((1, 1, S, D)).astype(np.float32) for _ in range(4))
+    scale = D ** -0.5
+    t0 = time.perf_counter()
+    o, lse = oracle.flash_attn2_fwd(q, k, v, scale, True)
+    oracle.flash_attn2_bwd(q, k, v, o, do, lse, scale, True)
+    dt = time.perf_counter() - t0
+    f, b = attn_flops(1, 1, S, D, True)
+    return dt, f + b
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: the reference's algorithm on the host cores.  The
+    reference itself (Rust DSL + absent compiler) cannot be built here, so
+    this times the oracle port; rank 0 only."""
+    if rank != 0:
+        return
+    import oracle
+
+    threads = oracle.max_threads()
+    for _ in range(max(args.warmup, 0) and 1):
+        cpu_attention_sample()
+    times = []
+    flops = 0.0
+    for _ in range(args.steps):
+        dt, flops = cpu_attention_sample()
+        times.append(dt)
+    mean = sum(times) / len(times)
+    value = flops / mean / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))", "impl": "reference",
+        "config": {"workload": "config#3 FA2 fwd+bwd causal B8 H32 S4096 D128",
+                   "sample_per_step": "1 of 256 (b,h) slices at full S=4096"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": "1 of 256 (b,h) slices of config #3 (fwd+bwd) per step; "
+                                   "throughput is per-slice FLOP / time (linear in B*H)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU legs
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-rope", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--small", action="store_true",
+                    help="profiling case: 2 of 8 batches (inputs still > L2)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import teenyformers_b200 as tfb
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peaks, peak_src = load_peaks()
+    B, H, S, D = CFG3["batch"], CFG3["heads"], CFG3["seq"], CFG3["head_dim"]
+    if args.small:
+        B = 2
+    BH = B * H
+    assert BH % world == 0, "heads must split evenly across ranks"
+    bh_local = BH // world
+    scale = D ** -0.5
+    fwd_flops_total, bwd_flops_total = attn_flops(B, H, S, D, True)
+    fwd_flops_rank = fwd_flops_total / world
+    bwd_flops_rank = bwd_flops_total / world
+
+    # ---- inputs: this rank's heads, seeded by global head range ----
+    g = torch.Generator(device=dev).manual_seed(42 + rank)
+    shape = (1, bh_local, S, D)
+    q, k, v, do = (torch.randn(shape, generator=g, device=dev, dtype=torch.bfloat16)
+                   for _ in range(4))
+    o = torch.empty_like(q)
+    lse = torch.empty((1, bh_local, S), device=dev, dtype=torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws = tfb.bwd_workspace(q)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        tfb.flash_attn2_fwd(q, k, v, scale, True, out=o, lse=lse)
+        tfb.flash_attn2_bwd(q, k, v, o, lse, do, scale, True, workspace=ws, grads=(dq, dk, dv))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if tfb.device_status(clear=True) != 0:
+        raise RuntimeError("device-side wait timed out during warm-up")
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = [int(x) for x in vis.split(",")] if vis else list(range(max(world, 1)))
+    sampler = ClockSampler(phys[:world] if world > 1 else [phys[local_rank] if vis else local_rank])
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+
+    # ---- timed region: K steps of fwd + bwd ----
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        tfb.flash_attn2_fwd(q, k, v, scale, True, out=o, lse=lse)
+        ev[i][1].record(stream)
+        tfb.flash_attn2_bwd(q, k, v, o, lse, do, scale, True, workspace=ws, grads=(dq, dk, dv))
+        ev[i][2].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    total_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    fwd_ms = max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps)
+    bwd_ms = max_over_ranks(sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps)
+    ms_per_step = total_ms / args.steps
+    value = (fwd_flops_total + bwd_flops_total) / (ms_per_step * 1e-3) / 1e12
+    fwd_tflops_rank = fwd_flops_rank / (fwd_ms * 1e-3) / 1e12
+    bwd_tflops_rank = bwd_flops_rank / (bwd_ms * 1e-3) / 1e12
+    status = tfb.device_status(clear=True)
+
+    # ---- RoPE + transpose leg (config #2, every rank runs the full config) ----
+    rope = None
+    if not args.no_rope:
+        rb, rs, rh, rd = CFG2["batch"], CFG2["seq"], CFG2["heads"], CFG2["head_dim"]
+        n_bufs = 4  # 4 x 128 MiB of in+out rotates through the 126 MB L2
+        xs = [torch.randn((rb, rs, rh, rd), generator=g, device=dev, dtype=torch.bfloat16)
+              for _ in range(n_bufs)]
+        ys = [torch.empty((rb, rh, rs, rd), device=dev, dtype=torch.bfloat16)
+              for _ in range(n_bufs)]
+        for i in range(max(args.warmup, 3) * n_bufs):
+            tfb.rope_transpose(xs[i % n_bufs], CFG2["rope_base"], tfb.TF_ROPE_ROTATE_HALF,
+                               out=ys[i % n_bufs])
+        n_rope = max(args.steps, 20) * n_bufs
+        re = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(n_rope)]
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(n_rope):
+            re[i][0].record(stream)
+            tfb.rope_transpose(xs[i % n_bufs], CFG2["rope_base"], tfb.TF_ROPE_ROTATE_HALF,
+                               out=ys[i % n_bufs])
+            re[i][1].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        rope_us = max_over_ranks(sum(a.elapsed_time(b) for a, b in re) / n_rope * 1e3)
+        rope_bytes = 2 * rb * rs * rh * rd * 2
+        rope_gbs = rope_bytes / (rope_us * 1e-6) / 1e9
+        rope = {"gbs_per_gpu": rope_gbs, "us_per_launch": rope_us, "bytes_per_launch": rope_bytes,
+                "frac_of_hbm": rope_gbs / peaks["hbm_gbs"],
+                "workload": "config#2 x[4,2048,32,128] bf16 -> RoPE(rotate-half, theta 1e4) -> "
+                            "[4,32,2048,128]; 4 rotating buffer sets (512 MiB) so reads miss L2"}
+        del xs, ys
+
+    clocks = sampler.stop() if rank == 0 else None
+
+    # ---- end to end through the public API, host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
+        outs_h = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (o, lse, dq, dk, dv)]
+        n_e2e = max(3, min(args.steps, 10))
+
+        def e2e_step():
+            dq_, dk_, dv_ = (torch.empty_like(t, device=dev) for t in (q, k, v))
+            q_d = hq.to(dev, non_blocking=True)
+            k_d = hk.to(dev, non_blocking=True)
+            v_d = hv.to(dev, non_blocking=True)
+            do_d = hdo.to(dev, non_blocking=True)
+            o_d, lse_d = tfb.flash_attn2_fwd(q_d, k_d, v_d, scale, True)
+            grads = tfb.flash_attn2_bwd(q_d, k_d, v_d, o_d, lse_d, do_d, scale, True,
+                                        workspace=ws, grads=(dq_, dk_, dv_))
+            for h_t, d_t in zip(outs_h, (o_d, lse_d) + tuple(grads)):
+                h_t.copy_(d_t, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(a.elapsed_time(b) / n_e2e)
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo)) * world
+        d2h = sum(t.numel() * t.element_size() for t in outs_h) * world
+        e2e = {"value": (fwd_flops_total + bwd_flops_total) / (e2e_ms * 1e-3) / 1e12,
+               "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": e2e_ms, "steps": n_e2e,
+               "path": "pinned host Q,K,V,dO -> flash_attn2_fwd/bwd (C ABI) -> pinned host "
+                       "O,LSE,dQ,dK,dV"}
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+
+        cpu_attention_sample()  # warm caches / thread pool
+        dts = []
+        fl = 0.0
+        for _ in range(2):
+            dt, fl = cpu_attention_sample()
+            dts.append(dt)
+        dt = min(dts)
+        cpu = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": oracle.max_threads(),
+               "kind": "port",
+               "sample": "1 of 256 (b,h) slices of config #3 at full S=4096 (causal fwd+bwd, "
+                         f"{dt:.2f} s), best of 2; throughput linear in B*H"}
+
+    if rank == 0:
+        traffic = load_traffic()
+        bf16_peak = peaks["bf16_tflops_sustained"]
+        fwd_ach = fwd_tflops_rank
+        bwd_ach = bwd_tflops_rank
+        dominant = "fa_bwd" if bwd_ms >= fwd_ms else "fa_fwd"
+        roof_fwd = {"kernel": "fa_fwd_sm100_kernel<128>", "bound": "tensor", "achieved": fwd_ach,
+                    "peak": bf16_peak, "unit": "TFLOP/s", "frac": fwd_ach / bf16_peak,
+                    "frac_of_burst": fwd_ach / peaks["bf16_tflops"],
+                    "traffic": traffic.get("fa_fwd"),
+                    "flops_per_launch": fwd_flops_rank, "ms_per_launch": fwd_ms}
+        roof_bwd = {"kernel": "fa_bwd (prep + dK/dV + dQ kernels, one C-ABI call)",
+                    "bound": "tensor", "achieved": bwd_ach, "peak": bf16_peak,
+                    "unit": "TFLOP/s", "frac": bwd_ach / bf16_peak,
+                    "frac_of_burst": bwd_ach / peaks["bf16_tflops"],
+                    "traffic": traffic.get("fa_bwd"),
+                    "flops_per_launch": bwd_flops_rank, "ms_per_launch": bwd_ms}
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1), torch generator on device)",
+            "config": {"workload": f"config#3 FA2 fwd+bwd causal B{B} H{H} S{S} D{D}"
+                                   + (" (small profiling case)" if args.small else ""),
+                       "batch": B, "heads": H, "seq_len": S, "head_dim": D,
+                       "heads_per_gpu": bh_local, "parallelism": f"bh-shard x{world}",
+                       "l2": "inputs larger than L2 (each of Q,K,V,dO is "
+                             f"{q.numel() * 2 / 2**20:.0f} MiB per GPU)"},
+            "fwd_tflops": fwd_flops_total / (fwd_ms * 1e-3) / 1e12,
+            "bwd_tflops": bwd_flops_total / (bwd_ms * 1e-3) / 1e12,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+            "roofline": roof_bwd if dominant == "fa_bwd" else roof_fwd,
+            "roofline_all": [roof_fwd, roof_bwd],
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json: bf16 sustained "
+                           f"{peaks['bf16_tflops_sustained']}, burst {peaks['bf16_tflops']} "
+                           f"TFLOP/s, HBM {peaks['hbm_gbs']} GB/s)",
+            "rope": rope,
+            "rope_gbs": rope["gbs_per_gpu"] if rope else None,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": 4 * args.steps,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

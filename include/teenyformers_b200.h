@@ -1,0 +1,150 @@
+/*
+ * teenyformers_b200.h -- C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Drop-in boundary for teenyformers' attention custom ops.  In the reference
+ * every op is a CustomOp/RuntimeOp pair whose kernel is reached through a
+ * generated `extern "C" fn entry_point(<ptrs>, <i32s>, <f32s>)` and launched
+ * by the external executor with grid()/block() and visitor-packed arguments
+ * (src/kernels/flash_attn2.rs:284-575, src/kernels/rope.rs:148-281,
+ * src/kernels/transpose_heads.rs:100-312).  The entry points below replace
+ * those launches: same pointer order and argument meaning, plus the shape
+ * values the reference passes through grid() (BH, head_dim) and a stream.
+ *
+ * Conventions (all entry points):
+ *   - plain device pointers, caller-owned; nothing here allocates device
+ *     memory.  Pointers must be 16-byte aligned (bf16 paths) or 4-byte
+ *     aligned (fp32 paths).
+ *   - stream-ordered on `stream` (a cudaStream_t; NULL = legacy default).
+ *   - return 0 (TF_OK) on success, a negative tf_status on invalid input or
+ *     launch failure; they never abort the process.  An empty problem
+ *     (a zero batch/head/sequence extent) is a successful no-op.
+ *   - layouts are dense row-major; "BH" = batch * heads.
+ *   - bf16 tensors are passed as `void*` (IEEE bfloat16 bits), fp32 as float*.
+ */
+#ifndef TEENYFORMERS_B200_H
+#define TEENYFORMERS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TF_API __attribute__((visibility("default")))
+#else
+#define TF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tf_status {
+  TF_OK = 0,
+  TF_ERR_INVALID_ARG = -1,    /* null pointer, negative extent, bad enum */
+  TF_ERR_UNSUPPORTED = -2,    /* head_dim / GQA ratio outside what is built */
+  TF_ERR_MISALIGNED = -3,     /* pointer alignment below the requirement */
+  TF_ERR_CUDA = -4,           /* CUDA launch or driver error */
+  TF_ERR_TOO_LARGE = -5,      /* extents beyond 32-bit indexing / TMA limits */
+  TF_ERR_DEVICE_TIMEOUT = -6  /* a kernel's bounded wait expired (see tf_b200_device_status) */
+} tf_status;
+
+typedef enum tf_rope_style {
+  TF_ROPE_INTERLEAVED = 0, /* pairs (2k, 2k+1): the reference (rope.rs:21-26) */
+  TF_ROPE_ROTATE_HALF = 1  /* pairs (k, k + D/2) */
+} tf_rope_style;
+
+/* ---------------- library ---------------- */
+
+TF_API int tf_b200_version(void);
+TF_API const char* tf_b200_status_string(int status);
+/* Reads (and with clear != 0 resets) the device-side error word of the
+ * current device: 0, or the site code of the first kernel wait that timed
+ * out.  Synchronises the device. */
+TF_API int tf_b200_device_status(int clear);
+
+/* ---------------- flash attention, bf16, tcgen05 (sm_100a) ----------------
+ * Replaces FlashAttn2RuntimeOp / CausalFlashAttn2RuntimeOp launches
+ * (src/kernels/flash_attn2.rs:284-384 and :436-530), whose kernel ABI is
+ * entry_point(q, k, v, o, l, n_ctx_q, n_ctx_k, softmax_scale, neg_inf)
+ * (tests/snapshots/kernel_sources__causal_flash_attn2_fwd_source.snap:5).
+ *   q, o  [batch * n_heads_q,  n_ctx_q, head_dim] bf16
+ *   k, v  [batch * n_heads_kv, n_ctx_k, head_dim] bf16
+ *   lse   [batch * n_heads_q,  n_ctx_q] fp32: m + ln(l), natural log of the
+ *         scaled scores (the reference's `l` cache, flash_attn2.rs:120-122)
+ *   causal != 0: key k hidden from query q when k > q (top-left aligned,
+ *         flash_attn2.rs:103-107).
+ *   GQA: query head h uses KV head h / (n_heads_q / n_heads_kv); the
+ *   reference has MHA only (n_heads_kv == n_heads_q).
+ *   head_dim: 64 or 128. */
+TF_API int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const void* v, void* o,
+                                 float* lse, int batch, int n_heads_q, int n_heads_kv,
+                                 int n_ctx_q, int n_ctx_k, int head_dim, float softmax_scale,
+                                 int causal, void* stream);
+
+/* Backward.  Replaces the reference's pack_backward_args launch
+ * (q, k, v, o, do, l, dq, dk, dv, n_ctx_q, n_ctx_k, softmax_scale;
+ * src/kernels/flash_attn2.rs:492-519).  dq/dk/dv are fully written (the
+ * reference needs dK/dV zero-initialised for its atomics; this does not).
+ * `workspace` is caller-provided scratch of
+ * tf_b200_flash_attn2_bwd_workspace_size(...) bytes (per-row softmax
+ * statistics); it must stay untouched until the call's work completes. */
+TF_API size_t tf_b200_flash_attn2_bwd_workspace_size(int batch, int n_heads_q, int n_ctx_q);
+TF_API int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const void* v, const void* o,
+                                 const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                                 void* workspace, int batch, int n_heads_q, int n_heads_kv,
+                                 int n_ctx_q, int n_ctx_k, int head_dim, float softmax_scale,
+                                 int causal, void* stream);
+
+/* ---------------- flash attention, fp32, reference argument set ----------------
+ * Same tensors and argument order as the reference kernels
+ * flash_attn2_causal_fwd (flash_attn2.rs:61-72, plus `neg_inf`) and
+ * flash_attn2_causal_bwd / flash_attn2_backward (:135-150, :209-224), with
+ * the grid extents (bh) and head_dim made explicit.  head_dim <= 256.
+ * dk/dv are fully written (no zero-initialisation needed). */
+TF_API int tf_b200_flash_attn2_fwd_f32(const float* q, const float* k, const float* v, float* o,
+                                float* l, int bh, int head_dim, int n_ctx_q, int n_ctx_k,
+                                float softmax_scale, float neg_inf, int causal, void* stream);
+TF_API int tf_b200_flash_attn2_bwd_f32(const float* q, const float* k, const float* v, const float* o,
+                                const float* d_o, const float* l, float* dq, float* dk,
+                                float* dv, int bh, int head_dim, int n_ctx_q, int n_ctx_k,
+                                float softmax_scale, int causal, void* stream);
+
+/* ---------------- RoPE ----------------
+ * Replaces RopeRtOp (src/kernels/rope.rs:148-238), kernel ABI
+ * entry_point(x, y, n_ctx, ln_rope_base)
+ * (tests/snapshots/kernel_sources__rope_forward_source.snap:5).
+ *   x, y [bh, n_ctx, head_dim]; pos = row index within n_ctx.
+ *   ln_rope_base = ln(rope_base), pre-computed by the caller as in rope.rs:194.
+ *   inverse != 0: the backward rotation (rope_backward, rope.rs:104-140).
+ * x == y (in place) is allowed. */
+TF_API int tf_b200_rope_f32(const float* x, float* y, int bh, int n_ctx, int head_dim,
+                     float ln_rope_base, int style, int inverse, void* stream);
+TF_API int tf_b200_rope_bf16(const void* x, void* y, int bh, int n_ctx, int head_dim,
+                      float ln_rope_base, int style, int inverse, void* stream);
+
+/* Fused transpose + RoPE (the attention layer's TransposeHeadsOp -> RopeOp,
+ * src/layers/attention.rs:97-123), batched:
+ *   inverse == 0: x [batch, seq_len, n_heads, head_dim] -> y [batch, n_heads, seq_len, head_dim]
+ *   inverse != 0: x [batch, n_heads, seq_len, head_dim] -> y [batch, seq_len, n_heads, head_dim]
+ *                 with the backward rotation (RopeOp backward then MergeHeads).
+ * x and y must not overlap. */
+TF_API int tf_b200_rope_transpose_bf16(const void* x, void* y, int batch, int seq_len, int n_heads,
+                                int head_dim, float ln_rope_base, int style, int inverse,
+                                void* stream);
+
+/* ---------------- head transpose / merge (bit-exact copies) ----------------
+ * Replace TransposeHeads / MergeHeads (src/kernels/transpose_heads.rs:100-165,
+ * :207-273), kernel ABI entry_point(src, dst, seq_len, n_heads)
+ * (tests/snapshots/kernel_sources__transpose_heads_source.snap:5), batched:
+ *   transpose: src [batch, seq_len, n_heads * head_dim] -> dst [batch, n_heads, seq_len, head_dim]
+ *   merge:     src [batch, n_heads, seq_len, head_dim] -> dst [batch, seq_len, n_heads * head_dim]
+ * elem_bytes: 2 (bf16/f16) or 4 (fp32); any bit pattern is copied unchanged. */
+TF_API int tf_b200_transpose_heads(const void* src, void* dst, int batch, int seq_len, int n_heads,
+                            int head_dim, int elem_bytes, void* stream);
+TF_API int tf_b200_merge_heads(const void* src, void* dst, int batch, int seq_len, int n_heads,
+                        int head_dim, int elem_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TEENYFORMERS_B200_H */

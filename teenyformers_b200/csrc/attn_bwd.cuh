@@ -1,0 +1,554 @@
+// attn_bwd.cuh -- flash-attention-2 backward for sm_100a (bf16 in/out, fp32 acc).
+//
+// Gradients of teenyformers' flash_attn2_causal_bwd / flash_attn2_backward
+// (src/kernels/flash_attn2.rs:135-279):
+//   D_q  = rowsum(O_q * dO_q)                       (:171)
+//   P    = exp(Q K^T * scale - LSE), future keys 0  (:186-189, top-left k > q)
+//   dS   = P * (dO V^T - D_q)                       (:191-192)
+//   dQ   = dS K * scale,  dK = dS^T Q * scale,  dV = P^T dO   (:194-197)
+// The reference adds dK/dV with per-(q,k) fp32 atomics; here they are
+// accumulated on chip, so the result is deterministic and dK/dV need no
+// zero-initialisation.
+//
+// Three kernels, all single-CTA tcgen05 (no clusters, no multicast):
+//  1. fa_bwd_prep_kernel: D_q and LSE*log2(e) per query row into the
+//     workspace ([BHq, Sq_pad] each, padded rows get D=0, LSE=+inf so
+//     their P is exactly 0).
+//  2. fa_bwd_dkdv_sm100_kernel: one CTA per 128-key tile of one KV head,
+//     looping over the 128-row query tiles of every query head of the GQA
+//     group.  TMEM: S^T [0,128), dP^T [128,256), dV [256,256+D),
+//     dK [256+D, 256+2D).  P^T and dS^T (bf16) overwrite the first 64
+//     columns of S^T / dP^T and feed dV += P^T dO, dK += dS^T Q straight
+//     from TMEM.
+//  3. fa_bwd_dq_sm100_kernel: one CTA per 128-row query tile, looping over
+//     key tiles: S, dP in TMEM, dS (bf16) over S, dQ += dS K.
+// Roles: warps 0-3 elementwise (one TMEM lane = one row per thread),
+// warp 4 MMA issuer, warp 5 TMA producer.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace tfb {
+
+inline long long bwd_sq_pad(int Sq) { return ((long long)Sq + 127) / 128 * 128; }
+inline size_t bwd_workspace_bytes(long long bhq, int Sq) {
+  return (size_t)(2 * bhq * bwd_sq_pad(Sq) * 4);
+}
+
+// ------------------------------------------------------------------ prep
+// grid = ceil(BHq * Sq_pad / 16), block 256: 16 threads per row, 8 elements
+// (16 bytes) each; requires D % 128 == 0 or D == 64.
+template <int D>
+__global__ void __launch_bounds__(256)
+    fa_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
+                       const float* __restrict__ lse, float* __restrict__ ws_lse2,
+                       float* __restrict__ ws_delta, int Sq, int Sq_pad, long long rows) {
+  constexpr int TPR = 16;  // threads per row
+  const long long row = (long long)blockIdx.x * (256 / TPR) + threadIdx.x / TPR;
+  const int sub = threadIdx.x % TPR;
+  if (row >= rows) return;
+  const long long bh = row / Sq_pad;
+  const int qi = (int)(row % Sq_pad);
+  float acc = 0.0f;
+  if (qi < Sq) {
+    const uint4* po = reinterpret_cast<const uint4*>(o + ((size_t)bh * Sq + qi) * D);
+    const uint4* pd = reinterpret_cast<const uint4*>(dO + ((size_t)bh * Sq + qi) * D);
+#pragma unroll
+    for (int v = sub; v < D / 8; v += TPR) {
+      const uint4 a = po[v], g = pd[v];
+      const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wg[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc += __uint_as_float(wa[i] << 16) * __uint_as_float(wg[i] << 16);
+        acc += __uint_as_float(wa[i] & 0xFFFF0000u) * __uint_as_float(wg[i] & 0xFFFF0000u);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (sub == 0) {
+    ws_delta[row] = acc;
+    ws_lse2[row] = qi < Sq ? lse[(size_t)bh * Sq + qi] * 1.4426950408889634f : INFINITY;
+  }
+}
+
+// ------------------------------------------------------------------ shared config
+struct BwdParams {
+  __nv_bfloat16* dq;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  const float* ws_lse2;
+  const float* ws_delta;
+  int Sq, Sk, Sq_pad;
+  int Hq, Hkv;
+  int BHq, BHkv;
+  int n_qt, n_kt;
+  float scale;       // softmax scale (natural)
+  float scale_log2;  // scale * log2(e)
+  int causal;
+};
+
+__device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_wait_noabort(uint32_t bar, uint32_t parity, int site) {
+  int dummy = 0;
+  (void)mbar_wait(bar, parity, (volatile int*)&dummy, site);
+}
+
+template <int D>
+struct BwdKvCfg {
+  static constexpr int kThreads = 192;
+  static constexpr int HALVES = D / 64;
+  static constexpr int HALF_BYTES = 128 * 128;
+  static constexpr int TILE_BYTES = 128 * D * 2;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + TILE_BYTES;
+  static constexpr int OFF_STAGE = OFF_V + TILE_BYTES;  // 2 stages of {Q, dO, lse2, delta}
+  static constexpr int STAGE_Q = 0;
+  static constexpr int STAGE_DO = TILE_BYTES;
+  static constexpr int STAGE_LSE = 2 * TILE_BYTES;
+  static constexpr int STAGE_DELTA = 2 * TILE_BYTES + 512;
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES + 1024;
+  static constexpr int OFF_BAR = OFF_STAGE + 2 * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t TM_ST = 0, TM_DPT = 128, TM_DV = 256, TM_DK = 256 + D;
+  static constexpr uint32_t TM_COLS = 512;
+};
+
+template <int D>
+struct BwdQCfg {
+  static constexpr int kThreads = 192;
+  static constexpr int HALVES = D / 64;
+  static constexpr int HALF_BYTES = 128 * 128;
+  static constexpr int TILE_BYTES = 128 * D * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = TILE_BYTES;
+  static constexpr int OFF_STAGE = 2 * TILE_BYTES;  // 2 stages of {K, V}
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_STAGE + 2 * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DQ = 256;
+  static constexpr uint32_t TM_COLS = 512;
+};
+
+enum BwdKvBar { KB_KV = 0, KB_QFULL = 1, KB_QEMPTY = 3, KB_SFULL = 5, KB_PFULL = 6,
+                KB_ACC = 7, KB_DRAIN = 8, KB_COUNT = 9 };
+enum BwdQBar { QB_Q = 0, QB_KVFULL = 1, QB_KVEMPTY = 3, QB_SFULL = 5, QB_PFULL = 6,
+               QB_ACC = 7, QB_DRAIN = 8, QB_COUNT = 9 };
+
+// Stores one 32-column fp32 TMEM chunk (scaled) as 32 bf16 to global.
+__device__ __forceinline__ void store_row_chunk_bf16(__nv_bfloat16* dst, const uint32_t (&r)[32],
+                                                     float mul) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    w[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * mul, __uint_as_float(r[2 * i + 1]) * mul);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+}
+
+// ------------------------------------------------------------------ dK / dV
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_do,
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, const BwdParams p) {
+  using C = BwdKvCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + KB_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Heavy first: key tile 0 has the most query tiles under the causal mask.
+  const int kt = blockIdx.x / p.BHkv;
+  const int bh_kv = blockIdx.x % p.BHkv;
+  const int b = bh_kv / p.Hkv, hk = bh_kv % p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  const int k0 = kt * 128;
+  const int qt_first = p.causal ? min(kt, p.n_qt) : 0;  // query tile i sees keys iff i >= kt
+  const int qt_per_head = p.n_qt - qt_first;
+  const int n_tiles = G * qt_per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(KB_KV), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(KB_QFULL + s), 1);
+      mbar_init(bar(KB_QEMPTY + s), 1);
+    }
+    mbar_init(bar(KB_SFULL), 1);
+    mbar_init(bar(KB_PFULL), 128);
+    mbar_init(bar(KB_ACC), 1);
+    mbar_init(bar(KB_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), C::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 5) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      int issued[2] = {0, 0};
+      bool ok = true;
+      mbar_arrive_expect_tx(bar(KB_KV), 2 * C::TILE_BYTES);
+      for (int hh = 0; hh < C::HALVES; ++hh) {
+        tma_load_3d(sbase + C::OFF_K + hh * C::HALF_BYTES, &tm_k, bar(KB_KV), hh * 64, k0, bh_kv);
+        tma_load_3d(sbase + C::OFF_V + hh * C::HALF_BYTES, &tm_v, bar(KB_KV), hh * 64, k0, bh_kv);
+      }
+      for (int it = 0; it < n_tiles && ok; ++it) {
+        const int st = it & 1, u = it >> 1;
+        if (u > 0) ok = mbar_wait(bar(KB_QEMPTY + st), (u - 1) & 1, abort_flag, 401);
+        if (!ok) break;
+        const int g = it / qt_per_head;
+        const int qi = qt_first + it % qt_per_head;
+        const int bh_q = b * p.Hq + hk * G + g;
+        const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(bar(KB_QFULL + st), 2 * C::TILE_BYTES + 1024);
+        for (int hh = 0; hh < C::HALVES; ++hh) {
+          tma_load_3d(sb + C::STAGE_Q + hh * C::HALF_BYTES, &tm_q, bar(KB_QFULL + st), hh * 64,
+                      qi * 128, bh_q);
+          tma_load_3d(sb + C::STAGE_DO + hh * C::HALF_BYTES, &tm_do, bar(KB_QFULL + st),
+                      hh * 64, qi * 128, bh_q);
+        }
+        const size_t ws_off = (size_t)bh_q * p.Sq_pad + (size_t)qi * 128;
+        bulk_load(sb + C::STAGE_LSE, p.ws_lse2 + ws_off, 512, bar(KB_QFULL + st));
+        bulk_load(sb + C::STAGE_DELTA, p.ws_delta + ws_off, 512, bar(KB_QFULL + st));
+        ++issued[st];
+      }
+      if (!ok) {
+        mbar_wait_noabort(bar(KB_KV), 0, 402);
+        for (int s = 0; s < 2; ++s)
+          if (issued[s]) mbar_wait_noabort(bar(KB_QFULL + s), (issued[s] - 1) & 1, 402);
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);
+      bool ok = mbar_wait(bar(KB_KV), 0, abort_flag, 411);
+      for (int it = 0; it < n_tiles && ok; ++it) {
+        const int st = it & 1;
+        ok = mbar_wait(bar(KB_QFULL + st), (it >> 1) & 1, abort_flag, 412);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + C::TM_ST, make_sdesc_sw128(sbase + C::OFF_K + off, 16, 1024),
+                 make_sdesc_sw128(sb + C::STAGE_Q + off, 16, 1024), idesc_s, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + C::TM_DPT, make_sdesc_sw128(sbase + C::OFF_V + off, 16, 1024),
+                 make_sdesc_sw128(sb + C::STAGE_DO + off, 16, 1024), idesc_s, kk > 0);
+        }
+        tc_commit(bar(KB_SFULL));
+        ok = mbar_wait(bar(KB_PFULL), it & 1, abort_flag, 413);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_ts(tmem + C::TM_DV, tmem + C::TM_ST + kk * 8,
+                 make_sdesc_sw128(sb + C::STAGE_DO + kk * 2048, C::HALF_BYTES, 1024), idesc_acc,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_ts(tmem + C::TM_DK, tmem + C::TM_DPT + kk * 8,
+                 make_sdesc_sw128(sb + C::STAGE_Q + kk * 2048, C::HALF_BYTES, 1024), idesc_acc,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(bar(KB_QEMPTY + st));
+      }
+      if (ok) tc_commit(bar(KB_ACC));
+      tc_commit(bar(KB_DRAIN));
+      mbar_wait_noabort(bar(KB_DRAIN), 0, 414);
+    }
+  } else {
+    // ---------------- elementwise: warps 0-3, thread = key row ----------------
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    const int key = k0 + row;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (int it = 0; it < n_tiles && ok; ++it) {
+      const int st = it & 1;
+      const int qi = qt_first + it % qt_per_head;
+      ok = mbar_wait(bar(KB_SFULL), it & 1, abort_flag, 421);
+      if (ok) ok = mbar_wait(bar(KB_QFULL + st), (it >> 1) & 1, abort_flag, 422);
+      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+      if (!ok) break;
+      tc_fence_after();
+      const uint8_t* sb = smem + C::OFF_STAGE + st * C::STAGE_BYTES;
+      const float* s_lse = reinterpret_cast<const float*>(sb + C::STAGE_LSE);
+      const float* s_delta = reinterpret_cast<const float*>(sb + C::STAGE_DELTA);
+      const bool diag = p.causal && qi * 128 < k0 + 127;
+      const int qlim = key - qi * 128;  // columns with index < qlim are hidden (k > q)
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_base + C::TM_ST + c * 32, sr);
+        tmem_ld32(tmem + lane_base + C::TM_DPT + c * 32, dr);
+        tmem_wait_ld();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c0 = c * 32 + 2 * i;
+          float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -s_lse[c0]));
+          float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -s_lse[c0 + 1]));
+          if (diag) {
+            if (c0 < qlim) p0 = 0.0f;
+            if (c0 + 1 < qlim) p1 = 0.0f;
+          }
+          const float d0 = p0 * (__uint_as_float(dr[2 * i]) - s_delta[c0]);
+          const float d1 = p1 * (__uint_as_float(dr[2 * i + 1]) - s_delta[c0 + 1]);
+          pk[i] = pack_bf16x2(p0, p1);
+          dk[i] = pack_bf16x2(d0, d1);
+        }
+        tmem_st16(tmem + lane_base + C::TM_ST + c * 16, pk);
+        tmem_st16(tmem + lane_base + C::TM_DPT + c * 16, dk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(KB_PFULL));
+    }
+    // ---- epilogue: dV = acc, dK = acc * scale ----
+    const bool valid = key < p.Sk;
+    __nv_bfloat16* dv_row = p.dv + ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D;
+    __nv_bfloat16* dk_row = p.dk + ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D;
+    if (n_tiles == 0) {
+      if (valid) {
+        uint4* a = reinterpret_cast<uint4*>(dv_row);
+        uint4* bb = reinterpret_cast<uint4*>(dk_row);
+        for (int v4 = 0; v4 < D / 8; ++v4) a[v4] = bb[v4] = make_uint4(0, 0, 0, 0);
+      }
+    } else if (__all_sync(0xffffffffu, ok && mbar_wait(bar(KB_ACC), 0, abort_flag, 423))) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + C::TM_DV + c * 32, r);
+        tmem_wait_ld();
+        if (valid) store_row_chunk_bf16(dv_row + c * 32, r, 1.0f);
+        tmem_ld32(tmem + lane_base + C::TM_DK + c * 32, r);
+        tmem_wait_ld();
+        if (valid) store_row_chunk_bf16(dk_row + c * 32, r, p.scale);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ dQ
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                           const __grid_constant__ CUtensorMap tm_do,
+                           const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v, const BwdParams p) {
+  using C = BwdQCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + QB_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  int qi = blockIdx.x / p.BHq;
+  const int bh = blockIdx.x % p.BHq;
+  if (p.causal) qi = p.n_qt - 1 - qi;  // heavy first
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
+  const int q0 = qi * 128;
+  int n_kv = p.n_kt;
+  if (p.causal) n_kv = min(p.n_kt, (min(p.Sq, q0 + 128) - 1) / 128 + 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(QB_Q), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(QB_KVFULL + s), 1);
+      mbar_init(bar(QB_KVEMPTY + s), 1);
+    }
+    mbar_init(bar(QB_SFULL), 1);
+    mbar_init(bar(QB_PFULL), 128);
+    mbar_init(bar(QB_ACC), 1);
+    mbar_init(bar(QB_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), C::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 5) {
+    if (lane == 0) {
+      int issued[2] = {0, 0};
+      bool ok = true;
+      mbar_arrive_expect_tx(bar(QB_Q), 2 * C::TILE_BYTES);
+      for (int hh = 0; hh < C::HALVES; ++hh) {
+        tma_load_3d(sbase + C::OFF_Q + hh * C::HALF_BYTES, &tm_q, bar(QB_Q), hh * 64, q0, bh);
+        tma_load_3d(sbase + C::OFF_DO + hh * C::HALF_BYTES, &tm_do, bar(QB_Q), hh * 64, q0, bh);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1, u = j >> 1;
+        if (u > 0) ok = mbar_wait(bar(QB_KVEMPTY + st), (u - 1) & 1, abort_flag, 501);
+        if (!ok) break;
+        const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(bar(QB_KVFULL + st), 2 * C::TILE_BYTES);
+        for (int hh = 0; hh < C::HALVES; ++hh) {
+          tma_load_3d(sb + hh * C::HALF_BYTES, &tm_k, bar(QB_KVFULL + st), hh * 64, j * 128,
+                      bh_kv);
+          tma_load_3d(sb + C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v, bar(QB_KVFULL + st),
+                      hh * 64, j * 128, bh_kv);
+        }
+        ++issued[st];
+      }
+      if (!ok) {
+        mbar_wait_noabort(bar(QB_Q), 0, 502);
+        for (int s = 0; s < 2; ++s)
+          if (issued[s]) mbar_wait_noabort(bar(QB_KVFULL + s), (issued[s] - 1) & 1, 502);
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
+      bool ok = mbar_wait(bar(QB_Q), 0, abort_flag, 511);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1;
+        ok = mbar_wait(bar(QB_KVFULL + st), (j >> 1) & 1, abort_flag, 512);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sk = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
+        const uint32_t sv = sk + C::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + C::TM_S, make_sdesc_sw128(sbase + C::OFF_Q + off, 16, 1024),
+                 make_sdesc_sw128(sk + off, 16, 1024), idesc_s, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + C::TM_DP, make_sdesc_sw128(sbase + C::OFF_DO + off, 16, 1024),
+                 make_sdesc_sw128(sv + off, 16, 1024), idesc_s, kk > 0);
+        }
+        tc_commit(bar(QB_SFULL));
+        ok = mbar_wait(bar(QB_PFULL), j & 1, abort_flag, 513);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_ts(tmem + C::TM_DQ, tmem + C::TM_S + kk * 8,
+                 make_sdesc_sw128(sk + kk * 2048, C::HALF_BYTES, 1024), idesc_dq,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(bar(QB_KVEMPTY + st));
+      }
+      if (ok) tc_commit(bar(QB_ACC));
+      tc_commit(bar(QB_DRAIN));
+      mbar_wait_noabort(bar(QB_DRAIN), 0, 514);
+    }
+  } else {
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    const int qrow = q0 + row;
+    const size_t ws_idx = (size_t)bh * p.Sq_pad + qrow;  // qrow < Sq_pad always
+    const float lse2 = p.ws_lse2[ws_idx];
+    const float delta = p.ws_delta[ws_idx];
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      ok = mbar_wait(bar(QB_SFULL), j & 1, abort_flag, 521);
+      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+      if (!ok) break;
+      tc_fence_after();
+      const int kb = j * 128;
+      const bool need_mask = (p.causal && kb + 127 > q0) || (kb + 128 > p.Sk);
+      int lim = p.Sk - 1 - kb;  // columns with index > lim are hidden
+      if (p.causal) lim = min(lim, qrow - kb);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_base + C::TM_S + c * 32, sr);
+        tmem_ld32(tmem + lane_base + C::TM_DP + c * 32, dr);
+        tmem_wait_ld();
+        uint32_t dsk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c0 = c * 32 + 2 * i;
+          float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -lse2));
+          float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -lse2));
+          if (need_mask) {
+            if (c0 > lim) p0 = 0.0f;
+            if (c0 + 1 > lim) p1 = 0.0f;
+          }
+          dsk[i] = pack_bf16x2(p0 * (__uint_as_float(dr[2 * i]) - delta),
+                               p1 * (__uint_as_float(dr[2 * i + 1]) - delta));
+        }
+        tmem_st16(tmem + lane_base + C::TM_S + c * 16, dsk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(QB_PFULL));
+    }
+    if (__all_sync(0xffffffffu, ok && mbar_wait(bar(QB_ACC), 0, abort_flag, 522))) {
+      tc_fence_after();
+      const bool valid = qrow < p.Sq;
+      __nv_bfloat16* dq_row = p.dq + ((size_t)bh * p.Sq + (valid ? qrow : 0)) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + C::TM_DQ + c * 32, r);
+        tmem_wait_ld();
+        if (valid) store_row_chunk_bf16(dq_row + c * 32, r, p.scale);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TM_COLS);
+  }
+}
+
+}  // namespace tfb

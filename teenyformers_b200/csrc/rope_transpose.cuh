@@ -1,0 +1,158 @@
+// rope_transpose.cuh -- RoPE and the [B,S,H,D] <-> [B,H,S,D] head transpose.
+//
+// Reference kernels (teenyformers):
+//   rope_forward / rope_backward       src/kernels/rope.rs:57-140
+//   transpose_heads / merge_heads      src/kernels/transpose_heads.rs:49-96
+// The attention layer applies transpose_heads and then RoPE
+// (src/layers/attention.rs:97-123); the two commute per (s, h) row, so the
+// fused kernel reads a [B,S,H,D] row, rotates it and writes it to its
+// [B,H,S,D] place in one pass (and the inverse for the backward).
+//
+// Angles follow rope.rs:86-93: inv_freq_k = exp(k * (-2 ln(base) / D)),
+// theta = pos * inv_freq_k, pos = s.  Pairs are interleaved (2k, 2k+1) as in
+// the reference, or rotate-half (k, k + D/2).  Arithmetic in fp32.
+//
+// HBM-bound: every element is read once and written once with 16-byte
+// vector accesses; each row is a contiguous D*elem-byte run on both sides.
+// One CTA handles one position s for a block of (b, h) rows so that sin/cos
+// of that position are computed once per thread and reused across rows.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace tfb {
+
+enum RopeLayout { LAYOUT_BSHD = 0, LAYOUT_BHSD = 1 };
+
+template <typename T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+__device__ __forceinline__ void unpack16(const uint4& v, float (&f)[8], __nv_bfloat16) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ uint4 pack16(const float (&f)[8], __nv_bfloat16) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(f[2 * i + 1]), "f"(f[2 * i]));
+    w[i] = r;
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ void unpack16(const uint4& v, float (&f)[4], float) {
+  f[0] = __uint_as_float(v.x);
+  f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z);
+  f[3] = __uint_as_float(v.w);
+}
+__device__ __forceinline__ uint4 pack16(const float (&f)[4], float) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                    __float_as_uint(f[3]));
+}
+
+__device__ __forceinline__ size_t row_offset(int layout, int b, int s, int h, int S, int H) {
+  return layout == LAYOUT_BSHD ? ((size_t)b * S + s) * H + h : ((size_t)b * H + h) * S + s;
+}
+
+// grid = (S, ceil(B*H / rows_per_cta)), block = 256.
+// STYLE 0: interleaved pairs; 1: rotate-half.  INV: inverse rotation.
+template <typename T, int STYLE, bool INV>
+__global__ void __launch_bounds__(256)
+    rope_rows_kernel(const T* __restrict__ x, T* __restrict__ y, int B, int S, int H, int D,
+                     int in_layout, int out_layout, float coef, int rows_per_cta) {
+  constexpr int EPV = Vec16<T>::N;  // elements per 16-byte vector
+  const int s = blockIdx.x;
+  // vectors handled per thread per row: 1 (interleaved) or 2 (rotate-half)
+  const int cpr = STYLE == 0 ? D / EPV : D / (2 * EPV);
+  const int rows_per_pass = blockDim.x / cpr;
+  const int c = threadIdx.x % cpr;
+  const int r0 = threadIdx.x / cpr;
+  if (r0 >= rows_per_pass) return;
+  const int row_lo = blockIdx.y * rows_per_cta;
+  const int row_hi = min(B * H, row_lo + rows_per_cta);
+
+  // Angles for the pairs this thread owns (computed once, reused over rows).
+  constexpr int NP = STYLE == 0 ? EPV / 2 : EPV;
+  float cs[NP], sn[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int k = STYLE == 0 ? c * (EPV / 2) + i : c * EPV + i;
+    const float inv_freq = expf((float)k * coef);
+    const float theta = (float)s * inv_freq;
+    float sv, cv;
+    sincosf(theta, &sv, &cv);
+    cs[i] = cv;
+    sn[i] = INV ? -sv : sv;
+  }
+
+  const size_t row_elems = (size_t)D;
+#pragma unroll 4
+  for (int r = row_lo + r0; r < row_hi; r += rows_per_pass) {
+    const int b = r / H, h = r % H;
+    const T* src = x + row_offset(in_layout, b, s, h, S, H) * row_elems;
+    T* dst = y + row_offset(out_layout, b, s, h, S, H) * row_elems;
+    if (STYLE == 0) {
+      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src) + c);
+      float f[EPV];
+      unpack16(v, f, T());
+#pragma unroll
+      for (int i = 0; i < EPV / 2; ++i) {
+        const float a = f[2 * i], bb = f[2 * i + 1];
+        f[2 * i] = a * cs[i] - bb * sn[i];
+        f[2 * i + 1] = a * sn[i] + bb * cs[i];
+      }
+      __stcs(reinterpret_cast<uint4*>(dst) + c, pack16(f, T()));
+    } else {
+      const int half_vecs = D / (2 * EPV);
+      const uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(src) + c);
+      const uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(src) + c + half_vecs);
+      float f0[EPV], f1[EPV];
+      unpack16(v0, f0, T());
+      unpack16(v1, f1, T());
+#pragma unroll
+      for (int i = 0; i < EPV; ++i) {
+        const float a = f0[i], bb = f1[i];
+        f0[i] = a * cs[i] - bb * sn[i];
+        f1[i] = a * sn[i] + bb * cs[i];
+      }
+      __stcs(reinterpret_cast<uint4*>(dst) + c, pack16(f0, T()));
+      __stcs(reinterpret_cast<uint4*>(dst) + c + half_vecs, pack16(f1, T()));
+    }
+  }
+}
+
+// Pure copy between [B,S,H,D] and [B,H,S,D] (either direction), any element
+// size: bit-exact.  VEC = bytes moved per access (16, 8, 4, 2 or 1).
+template <typename V>
+__global__ void __launch_bounds__(256)
+    transpose_rows_kernel(const V* __restrict__ x, V* __restrict__ y, int B, int S, int H,
+                          int vecs_per_row, int in_layout, int out_layout, long long total) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % vecs_per_row);
+    const long long row = i / vecs_per_row;  // enumerated in the input layout
+    int b, s, h;
+    if (in_layout == LAYOUT_BSHD) {
+      h = (int)(row % H);
+      s = (int)((row / H) % S);
+      b = (int)(row / ((long long)H * S));
+    } else {
+      s = (int)(row % S);
+      h = (int)((row / S) % H);
+      b = (int)(row / ((long long)H * S));
+    }
+    const size_t out_row = row_offset(out_layout, b, s, h, S, H);
+    y[out_row * vecs_per_row + c] = x[(size_t)row * vecs_per_row + c];
+  }
+}
+
+}  // namespace tfb

@@ -1,0 +1,438 @@
+// tfb_lib.cu -- the C ABI (include/teenyformers_b200.h) over the sm_100a
+// kernels.  One translation unit: the kernels share the device status word.
+//
+// Every entry point validates shapes, pointers and alignment on the host and
+// returns a tf_status; nothing here allocates device memory or synchronises
+// (except tf_b200_device_status).  Global state is limited to per-device
+// one-time kernel attribute setup and the cached driver entry point for
+// tensor-map encoding, both initialised under std::call_once.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/teenyformers_b200.h"
+#include "sm100.cuh"
+#include "attn_fwd.cuh"
+#include "attn_bwd.cuh"
+#include "attn_f32.cuh"
+#include "rope_transpose.cuh"
+
+using namespace tfb;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+bool is_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TF_OK : TF_ERR_CUDA;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor map over [outer, rows, D] with a (64 x 128 x 1) box and
+// 128-byte swizzle: the K-major SW128 canonical layout the MMAs read.
+bool make_bf16_map(CUtensorMap* map, const void* base, int D, int rows, int outer,
+                   int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)outer};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)D * 2 * (cuuint64_t)rows};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r =
+      enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+
+// Raises the dynamic shared-memory limit of every kernel that needs more
+// than 48 KB, once per device.
+int ensure_device_setup() {
+  static std::once_flag flags[kMaxDevices];
+  static int status[kMaxDevices];
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return TF_ERR_CUDA;
+  std::call_once(flags[dev], [dev] {
+    cudaError_t e = cudaSuccess;
+    auto set = [&](const void* fn, int bytes) {
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    };
+    set((const void*)fa_fwd_sm100_kernel<64>, FwdCfg<64>::SMEM_BYTES);
+    set((const void*)fa_fwd_sm100_kernel<128>, FwdCfg<128>::SMEM_BYTES);
+    set((const void*)fa_bwd_dkdv_sm100_kernel<64>, BwdKvCfg<64>::SMEM_BYTES);
+    set((const void*)fa_bwd_dkdv_sm100_kernel<128>, BwdKvCfg<128>::SMEM_BYTES);
+    set((const void*)fa_bwd_dq_sm100_kernel<64>, BwdQCfg<64>::SMEM_BYTES);
+    set((const void*)fa_bwd_dq_sm100_kernel<128>, BwdQCfg<128>::SMEM_BYTES);
+    const int f32_max = (3 * kF32Rows + 3 * kF32Tile) * kF32MaxD * 4 + 2 * kF32Tile * 4;
+    set((const void*)fa_fwd_f32_kernel, f32_max);
+    set((const void*)fa_bwd_dq_f32_kernel, f32_max);
+    set((const void*)fa_bwd_dkdv_f32_kernel, f32_max);
+    status[dev] = e == cudaSuccess ? TF_OK : TF_ERR_CUDA;
+  });
+  return status[dev];
+}
+
+bool fits_i32(long long v) { return v >= 0 && v <= 0x7fffffffLL; }
+
+}  // namespace
+
+// ===================================================================== library
+extern "C" int tf_b200_version(void) { return 1; }
+
+extern "C" const char* tf_b200_status_string(int s) {
+  switch (s) {
+    case TF_OK: return "ok";
+    case TF_ERR_INVALID_ARG: return "invalid argument";
+    case TF_ERR_UNSUPPORTED: return "unsupported configuration";
+    case TF_ERR_MISALIGNED: return "misaligned pointer";
+    case TF_ERR_CUDA: return "CUDA error";
+    case TF_ERR_TOO_LARGE: return "problem too large";
+    case TF_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int tf_b200_device_status(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return TF_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tfb::g_device_status, sizeof(int)) != cudaSuccess)
+    return TF_ERR_CUDA;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(tfb::g_device_status, &zero, sizeof(int)) != cudaSuccess)
+      return TF_ERR_CUDA;
+  }
+  return v;
+}
+
+// ===================================================================== attention bf16
+extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const void* v,
+                                            void* o, float* lse, int batch, int n_heads_q,
+                                            int n_heads_kv, int n_ctx_q, int n_ctx_k,
+                                            int head_dim, float softmax_scale, int causal,
+                                            void* stream) {
+  if (batch < 0 || n_heads_q < 0 || n_heads_kv < 0 || n_ctx_q < 0 || n_ctx_k < 0)
+    return TF_ERR_INVALID_ARG;
+  if (batch == 0 || n_heads_q == 0 || n_ctx_q == 0) return TF_OK;
+  if (n_ctx_k == 0 || n_heads_kv == 0) return TF_ERR_INVALID_ARG;
+  if (n_heads_q % n_heads_kv != 0) return TF_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return TF_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !o || !lse) return TF_ERR_INVALID_ARG;
+  if (!is_aligned(q, 16) || !is_aligned(k, 16) || !is_aligned(v, 16) || !is_aligned(o, 16) ||
+      !is_aligned(lse, 4))
+    return TF_ERR_MISALIGNED;
+  if (!(softmax_scale > 0.0f) || !std::isfinite(softmax_scale)) return TF_ERR_INVALID_ARG;
+  const long long bhq = (long long)batch * n_heads_q;
+  const long long n_pairs = (n_ctx_q + 255) / 256;
+  if (!fits_i32(bhq) || !fits_i32(bhq * n_pairs) || !fits_i32((long long)batch * n_heads_kv))
+    return TF_ERR_TOO_LARGE;
+  if (int st = ensure_device_setup()) return st;
+
+  CUtensorMap tq, tk, tv;
+  if (!make_bf16_map(&tq, q, head_dim, n_ctx_q, (int)bhq, 128) ||
+      !make_bf16_map(&tk, k, head_dim, n_ctx_k, batch * n_heads_kv, 128) ||
+      !make_bf16_map(&tv, v, head_dim, n_ctx_k, batch * n_heads_kv, 128))
+    return TF_ERR_CUDA;
+  FwdParams prm;
+  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.lse = lse;
+  prm.Sq = n_ctx_q;
+  prm.Sk = n_ctx_k;
+  prm.Hq = n_heads_q;
+  prm.Hkv = n_heads_kv;
+  prm.BHq = (int)bhq;
+  prm.n_pairs = (int)n_pairs;
+  prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+  prm.causal = causal ? 1 : 0;
+  const dim3 grid((unsigned)(bhq * n_pairs));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 128)
+    fa_fwd_sm100_kernel<128><<<grid, FwdCfg<128>::kThreads, FwdCfg<128>::SMEM_BYTES, st>>>(
+        tq, tk, tv, prm);
+  else
+    fa_fwd_sm100_kernel<64><<<grid, FwdCfg<64>::kThreads, FwdCfg<64>::SMEM_BYTES, st>>>(
+        tq, tk, tv, prm);
+  return launch_status();
+}
+
+extern "C" size_t tf_b200_flash_attn2_bwd_workspace_size(int batch, int n_heads_q,
+                                                         int n_ctx_q) {
+  if (batch <= 0 || n_heads_q <= 0 || n_ctx_q <= 0) return 0;
+  return bwd_workspace_bytes((long long)batch * n_heads_q, n_ctx_q);
+}
+
+extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const void* v,
+                                            const void* o, const void* d_o, const float* lse,
+                                            void* dq, void* dk, void* dv, void* workspace,
+                                            int batch, int n_heads_q, int n_heads_kv,
+                                            int n_ctx_q, int n_ctx_k, int head_dim,
+                                            float softmax_scale, int causal, void* stream) {
+  if (batch < 0 || n_heads_q < 0 || n_heads_kv < 0 || n_ctx_q < 0 || n_ctx_k < 0)
+    return TF_ERR_INVALID_ARG;
+  if (batch == 0 || n_heads_q == 0 || (n_ctx_q == 0 && n_ctx_k == 0)) return TF_OK;
+  if (n_heads_kv == 0 || n_ctx_k == 0 || n_ctx_q == 0) return TF_ERR_INVALID_ARG;
+  if (n_heads_q % n_heads_kv != 0) return TF_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return TF_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !o || !d_o || !lse || !dq || !dk || !dv || !workspace)
+    return TF_ERR_INVALID_ARG;
+  if (!is_aligned(q, 16) || !is_aligned(k, 16) || !is_aligned(v, 16) || !is_aligned(o, 16) ||
+      !is_aligned(d_o, 16) || !is_aligned(dq, 16) || !is_aligned(dk, 16) ||
+      !is_aligned(dv, 16) || !is_aligned(lse, 4) || !is_aligned(workspace, 16))
+    return TF_ERR_MISALIGNED;
+  if (!(softmax_scale > 0.0f) || !std::isfinite(softmax_scale)) return TF_ERR_INVALID_ARG;
+  const long long bhq = (long long)batch * n_heads_q;
+  const long long bhkv = (long long)batch * n_heads_kv;
+  if (!fits_i32(bhq * ((n_ctx_q + 127) / 128)) || !fits_i32(bhkv * ((n_ctx_k + 127) / 128)) ||
+      !fits_i32(bhq * (long long)n_ctx_q))
+    return TF_ERR_TOO_LARGE;
+  if (int st = ensure_device_setup()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sq_pad = (int)bwd_sq_pad(n_ctx_q);
+  float* ws_lse2 = static_cast<float*>(workspace);
+  float* ws_delta = ws_lse2 + bhq * sq_pad;
+  const long long rows = bhq * sq_pad;
+  if (head_dim == 128)
+    fa_bwd_prep_kernel<128><<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(d_o), lse,
+        ws_lse2, ws_delta, n_ctx_q, sq_pad, rows);
+  else
+    fa_bwd_prep_kernel<64><<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(d_o), lse,
+        ws_lse2, ws_delta, n_ctx_q, sq_pad, rows);
+  if (int e = launch_status()) return e;
+
+  CUtensorMap tq, tdo, tk, tv;
+  if (!make_bf16_map(&tq, q, head_dim, n_ctx_q, (int)bhq, 128) ||
+      !make_bf16_map(&tdo, d_o, head_dim, n_ctx_q, (int)bhq, 128) ||
+      !make_bf16_map(&tk, k, head_dim, n_ctx_k, (int)bhkv, 128) ||
+      !make_bf16_map(&tv, v, head_dim, n_ctx_k, (int)bhkv, 128))
+    return TF_ERR_CUDA;
+  BwdParams prm;
+  prm.dq = static_cast<__nv_bfloat16*>(dq);
+  prm.dk = static_cast<__nv_bfloat16*>(dk);
+  prm.dv = static_cast<__nv_bfloat16*>(dv);
+  prm.ws_lse2 = ws_lse2;
+  prm.ws_delta = ws_delta;
+  prm.Sq = n_ctx_q;
+  prm.Sk = n_ctx_k;
+  prm.Sq_pad = sq_pad;
+  prm.Hq = n_heads_q;
+  prm.Hkv = n_heads_kv;
+  prm.BHq = (int)bhq;
+  prm.BHkv = (int)bhkv;
+  prm.n_qt = (n_ctx_q + 127) / 128;
+  prm.n_kt = (n_ctx_k + 127) / 128;
+  prm.scale = softmax_scale;
+  prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+  prm.causal = causal ? 1 : 0;
+  const dim3 grid_kv((unsigned)(bhkv * prm.n_kt));
+  const dim3 grid_q((unsigned)(bhq * prm.n_qt));
+  if (head_dim == 128) {
+    fa_bwd_dkdv_sm100_kernel<128><<<grid_kv, BwdKvCfg<128>::kThreads, BwdKvCfg<128>::SMEM_BYTES,
+                                    st>>>(tq, tdo, tk, tv, prm);
+    fa_bwd_dq_sm100_kernel<128><<<grid_q, BwdQCfg<128>::kThreads, BwdQCfg<128>::SMEM_BYTES, st>>>(
+        tq, tdo, tk, tv, prm);
+  } else {
+    fa_bwd_dkdv_sm100_kernel<64><<<grid_kv, BwdKvCfg<64>::kThreads, BwdKvCfg<64>::SMEM_BYTES,
+                                   st>>>(tq, tdo, tk, tv, prm);
+    fa_bwd_dq_sm100_kernel<64><<<grid_q, BwdQCfg<64>::kThreads, BwdQCfg<64>::SMEM_BYTES, st>>>(
+        tq, tdo, tk, tv, prm);
+  }
+  return launch_status();
+}
+
+// ===================================================================== attention fp32
+extern "C" int tf_b200_flash_attn2_fwd_f32(const float* q, const float* k, const float* v,
+                                           float* o, float* l, int bh, int head_dim,
+                                           int n_ctx_q, int n_ctx_k, float softmax_scale,
+                                           float neg_inf, int causal, void* stream) {
+  if (bh < 0 || head_dim < 0 || n_ctx_q < 0 || n_ctx_k < 0) return TF_ERR_INVALID_ARG;
+  if (bh == 0 || n_ctx_q == 0 || head_dim == 0) return TF_OK;
+  if (n_ctx_k == 0) return TF_ERR_INVALID_ARG;
+  if (head_dim > kF32MaxD) return TF_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !o || !l) return TF_ERR_INVALID_ARG;
+  if (!is_aligned(q, 4) || !is_aligned(k, 4) || !is_aligned(v, 4) || !is_aligned(o, 4) ||
+      !is_aligned(l, 4))
+    return TF_ERR_MISALIGNED;
+  if (bh > 65535) return TF_ERR_TOO_LARGE;
+  if (int st = ensure_device_setup()) return st;
+  const dim3 grid((n_ctx_q + kF32Rows - 1) / kF32Rows, bh);
+  const int smem = (kF32Rows + 2 * kF32Tile) * head_dim * 4;
+  fa_fwd_f32_kernel<<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+      q, k, v, o, l, n_ctx_q, n_ctx_k, head_dim, softmax_scale, neg_inf, causal ? 1 : 0, 1, 1);
+  return launch_status();
+}
+
+extern "C" int tf_b200_flash_attn2_bwd_f32(const float* q, const float* k, const float* v,
+                                           const float* o, const float* d_o, const float* l,
+                                           float* dq, float* dk, float* dv, int bh,
+                                           int head_dim, int n_ctx_q, int n_ctx_k,
+                                           float softmax_scale, int causal, void* stream) {
+  if (bh < 0 || head_dim < 0 || n_ctx_q < 0 || n_ctx_k < 0) return TF_ERR_INVALID_ARG;
+  if (bh == 0 || head_dim == 0 || (n_ctx_q == 0 && n_ctx_k == 0)) return TF_OK;
+  if (n_ctx_q == 0 || n_ctx_k == 0) return TF_ERR_INVALID_ARG;
+  if (head_dim > kF32MaxD) return TF_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !o || !d_o || !l || !dq || !dk || !dv) return TF_ERR_INVALID_ARG;
+  if (bh > 65535) return TF_ERR_TOO_LARGE;
+  if (int st = ensure_device_setup()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 gq((n_ctx_q + kF32Rows - 1) / kF32Rows, bh);
+  const int smem_q = (3 * kF32Rows + 2 * kF32Tile) * head_dim * 4;
+  fa_bwd_dq_f32_kernel<<<gq, 256, smem_q, st>>>(q, k, v, o, d_o, l, dq, n_ctx_q, n_ctx_k,
+                                                head_dim, softmax_scale, causal ? 1 : 0, 1, 1);
+  const dim3 gk((n_ctx_k + kF32Rows - 1) / kF32Rows, bh);
+  const int smem_k = (2 * kF32Rows + 3 * kF32Tile) * head_dim * 4 + 2 * kF32Tile * 4;
+  fa_bwd_dkdv_f32_kernel<<<gk, 256, smem_k, st>>>(q, k, v, o, d_o, l, dk, dv, n_ctx_q, n_ctx_k,
+                                                  head_dim, softmax_scale, causal ? 1 : 0, 1,
+                                                  1);
+  return launch_status();
+}
+
+// ===================================================================== RoPE / transpose
+namespace {
+
+template <typename T>
+int launch_rope(const T* x, T* y, int B, int S, int H, int D, float ln_base, int style,
+                int inverse, int in_layout, int out_layout, cudaStream_t st) {
+  constexpr int EPV = Vec16<T>::N;
+  if (style != TF_ROPE_INTERLEAVED && style != TF_ROPE_ROTATE_HALF) return TF_ERR_INVALID_ARG;
+  if (D % (2 * EPV) != 0 || D > 2048) return TF_ERR_UNSUPPORTED;
+  if (!is_aligned(x, 16) || !is_aligned(y, 16)) return TF_ERR_MISALIGNED;
+  const long long rows = (long long)B * H;
+  if (!fits_i32(rows) || !fits_i32(rows * S) || S > 0x7fffffff) return TF_ERR_TOO_LARGE;
+  const int cpr = style == TF_ROPE_INTERLEAVED ? D / EPV : D / (2 * EPV);
+  if (cpr > 256) return TF_ERR_UNSUPPORTED;
+  const int rows_per_pass = 256 / cpr;
+  // Enough CTAs to fill the GPU: split the (b, h) rows of a position only
+  // when there are few positions.
+  const long long target = 148LL * 8;
+  long long per_cta = rows;
+  if (S < target) {
+    const long long split = (target + S - 1) / S;
+    per_cta = (rows + split - 1) / split;
+  }
+  per_cta = ((per_cta + rows_per_pass - 1) / rows_per_pass) * rows_per_pass;
+  const long long gy = (rows + per_cta - 1) / per_cta;
+  if (gy > 65535) return TF_ERR_TOO_LARGE;
+  const float coef = (-2.0f * ln_base) / (float)D;
+  const dim3 grid((unsigned)S, (unsigned)gy);
+#define TFB_ROPE_LAUNCH(STY, INV)                                                          \
+  rope_rows_kernel<T, STY, INV><<<grid, 256, 0, st>>>(x, y, B, S, H, D, in_layout, out_layout, \
+                                                      coef, (int)per_cta)
+  if (style == 0 && !inverse) TFB_ROPE_LAUNCH(0, false);
+  if (style == 0 && inverse) TFB_ROPE_LAUNCH(0, true);
+  if (style == 1 && !inverse) TFB_ROPE_LAUNCH(1, false);
+  if (style == 1 && inverse) TFB_ROPE_LAUNCH(1, true);
+#undef TFB_ROPE_LAUNCH
+  return launch_status();
+}
+
+int launch_transpose(const void* src, void* dst, int B, int S, int H, int D, int elem_bytes,
+                     int in_layout, int out_layout, cudaStream_t st) {
+  const long long row_bytes = (long long)D * elem_bytes;
+  int vec = 16;
+  while (vec > 1 && (row_bytes % vec != 0 || !is_aligned(src, vec) || !is_aligned(dst, vec)))
+    vec >>= 1;
+  if (!is_aligned(src, elem_bytes) || !is_aligned(dst, elem_bytes)) return TF_ERR_MISALIGNED;
+  const long long vpr = row_bytes / vec;
+  const long long total = (long long)B * S * H * vpr;
+  if (!fits_i32(vpr) || !fits_i32((long long)B * S) || !fits_i32((long long)B * H))
+    return TF_ERR_TOO_LARGE;
+  const long long blocks_needed = (total + 255) / 256;
+  const unsigned blocks = (unsigned)(blocks_needed < 148LL * 32 ? blocks_needed : 148LL * 32);
+#define TFB_TR(VT)                                                                       \
+  transpose_rows_kernel<VT><<<blocks, 256, 0, st>>>(static_cast<const VT*>(src),         \
+                                                    static_cast<VT*>(dst), B, S, H,      \
+                                                    (int)vpr, in_layout, out_layout, total)
+  switch (vec) {
+    case 16: TFB_TR(uint4); break;
+    case 8: TFB_TR(uint2); break;
+    case 4: TFB_TR(uint32_t); break;
+    case 2: TFB_TR(uint16_t); break;
+    default: TFB_TR(uint8_t); break;
+  }
+#undef TFB_TR
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" int tf_b200_rope_f32(const float* x, float* y, int bh, int n_ctx, int head_dim,
+                                float ln_rope_base, int style, int inverse, void* stream) {
+  if (bh < 0 || n_ctx < 0 || head_dim < 0) return TF_ERR_INVALID_ARG;
+  if (bh == 0 || n_ctx == 0 || head_dim == 0) return TF_OK;
+  if (!x || !y) return TF_ERR_INVALID_ARG;
+  return launch_rope<float>(x, y, 1, n_ctx, bh, head_dim, ln_rope_base, style, inverse,
+                            LAYOUT_BHSD, LAYOUT_BHSD, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_b200_rope_bf16(const void* x, void* y, int bh, int n_ctx, int head_dim,
+                                 float ln_rope_base, int style, int inverse, void* stream) {
+  if (bh < 0 || n_ctx < 0 || head_dim < 0) return TF_ERR_INVALID_ARG;
+  if (bh == 0 || n_ctx == 0 || head_dim == 0) return TF_OK;
+  if (!x || !y) return TF_ERR_INVALID_ARG;
+  return launch_rope<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x),
+                                    static_cast<__nv_bfloat16*>(y), 1, n_ctx, bh, head_dim,
+                                    ln_rope_base, style, inverse, LAYOUT_BHSD, LAYOUT_BHSD,
+                                    static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_b200_rope_transpose_bf16(const void* x, void* y, int batch, int seq_len,
+                                           int n_heads, int head_dim, float ln_rope_base,
+                                           int style, int inverse, void* stream) {
+  if (batch < 0 || seq_len < 0 || n_heads < 0 || head_dim < 0) return TF_ERR_INVALID_ARG;
+  if (batch == 0 || seq_len == 0 || n_heads == 0 || head_dim == 0) return TF_OK;
+  if (!x || !y || x == y) return TF_ERR_INVALID_ARG;
+  return launch_rope<__nv_bfloat16>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), batch, seq_len,
+      n_heads, head_dim, ln_rope_base, style, inverse, inverse ? LAYOUT_BHSD : LAYOUT_BSHD,
+      inverse ? LAYOUT_BSHD : LAYOUT_BHSD, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_b200_transpose_heads(const void* src, void* dst, int batch, int seq_len,
+                                       int n_heads, int head_dim, int elem_bytes,
+                                       void* stream) {
+  if (batch < 0 || seq_len < 0 || n_heads < 0 || head_dim < 0) return TF_ERR_INVALID_ARG;
+  if (elem_bytes != 2 && elem_bytes != 4) return TF_ERR_INVALID_ARG;
+  if (batch == 0 || seq_len == 0 || n_heads == 0 || head_dim == 0) return TF_OK;
+  if (!src || !dst || src == dst) return TF_ERR_INVALID_ARG;
+  return launch_transpose(src, dst, batch, seq_len, n_heads, head_dim, elem_bytes, LAYOUT_BSHD,
+                          LAYOUT_BHSD, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_b200_merge_heads(const void* src, void* dst, int batch, int seq_len,
+                                   int n_heads, int head_dim, int elem_bytes, void* stream) {
+  if (batch < 0 || seq_len < 0 || n_heads < 0 || head_dim < 0) return TF_ERR_INVALID_ARG;
+  if (elem_bytes != 2 && elem_bytes != 4) return TF_ERR_INVALID_ARG;
+  if (batch == 0 || seq_len == 0 || n_heads == 0 || head_dim == 0) return TF_OK;
+  if (!src || !dst || src == dst) return TF_ERR_INVALID_ARG;
+  return launch_transpose(src, dst, batch, seq_len, n_heads, head_dim, elem_bytes, LAYOUT_BHSD,
+                          LAYOUT_BSHD, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,306 @@
+"""Host-side mirror of teenyformers' attention-path custom ops, over the C ABI.
+
+The reference defines each op as a CustomOp (graph node: name, output-shape
+inference) plus a RuntimeOp (activation-input count, param-cache shapes,
+forward and backward launch).  The classes here keep those names, argument
+meanings and shape rules and launch the sm_100a kernels through
+``include/teenyformers_b200.h``; tensors are torch CUDA tensors (torch is the
+device-memory / stream plumbing only):
+
+  FlashAttn2Op        src/kernels/flash_attn2.rs:393-429 (non-causal)
+  CausalFlashAttn2Op  src/kernels/flash_attn2.rs:539-575
+  RopeOp              src/kernels/rope.rs:246-281
+  TransposeHeadsOp    src/kernels/transpose_heads.rs:168-203
+  MergeHeadsOp        src/kernels/transpose_heads.rs:276-312
+
+Errors: the reference asserts on bad shapes (src/layers/attention.rs:68);
+here a bad call raises ValueError (shape) or TfError (status from the C ABI).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _capi
+from ._capi import TF_ROPE_INTERLEAVED, TF_ROPE_ROTATE_HALF, TfError, call
+
+__all__ = [
+    "FlashAttn2Op", "CausalFlashAttn2Op", "RopeOp", "TransposeHeadsOp", "MergeHeadsOp",
+    "flash_attn2_fwd", "flash_attn2_bwd", "rope", "rope_transpose", "transpose_heads",
+    "merge_heads", "bwd_workspace", "TF_ROPE_INTERLEAVED", "TF_ROPE_ROTATE_HALF", "TfError",
+]
+
+
+def _ptr(t: torch.Tensor | None):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need(cond: bool, msg: str):
+    if not cond:
+        raise ValueError(msg)
+
+
+def _as4(x: torch.Tensor) -> torch.Tensor:
+    """[BH, S, D] (reference layout) -> [1, BH, S, D]; [B, H, S, D] unchanged."""
+    _need(x.dim() in (3, 4), f"expected [BH,S,D] or [B,H,S,D], got {tuple(x.shape)}")
+    return x.unsqueeze(0) if x.dim() == 3 else x
+
+
+# ----------------------------------------------------------------- functional API
+def flash_attn2_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float,
+                    causal: bool, out: torch.Tensor | None = None,
+                    lse: torch.Tensor | None = None):
+    """O, LSE of flash attention.  q [B,Hq,Sq,D] / k,v [B,Hkv,Sk,D] (or 3-D
+    [BH,S,D]); bf16 -> tcgen05 kernel, fp32 -> reference-ABI fp32 kernel."""
+    q4, k4, v4 = _as4(q), _as4(k), _as4(v)
+    B, Hq, Sq, D = q4.shape
+    Hkv, Sk = k4.shape[1], k4.shape[2]
+    _need(k4.shape == v4.shape and k4.shape[0] == B and k4.shape[3] == D, "k/v shape mismatch")
+    for t in (q, k, v):
+        _need(t.is_cuda and t.is_contiguous(), "inputs must be contiguous CUDA tensors")
+        _need(t.dtype == q.dtype, "q, k, v dtypes differ")
+    o = torch.empty_like(q) if out is None else out
+    l = torch.empty(q.shape[:-1], dtype=torch.float32, device=q.device) if lse is None else lse
+    if q.dtype == torch.bfloat16:
+        call("tf_b200_flash_attn2_fwd_bf16", _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(l), B, Hq,
+             Hkv, Sq, Sk, D, float(softmax_scale), int(bool(causal)), _stream(q))
+    elif q.dtype == torch.float32:
+        _need(Hq == Hkv, "the fp32 reference-ABI kernels are MHA only")
+        call("tf_b200_flash_attn2_fwd_f32", _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(l), B * Hq,
+             D, Sq, Sk, float(softmax_scale), float("-inf"), int(bool(causal)), _stream(q))
+    else:
+        raise ValueError(f"unsupported dtype {q.dtype}")
+    return o, l
+
+
+def bwd_workspace(q: torch.Tensor) -> torch.Tensor:
+    q4 = _as4(q)
+    B, Hq, Sq, _ = q4.shape
+    n = _capi.raw("tf_b200_flash_attn2_bwd_workspace_size", B, Hq, Sq)
+    return torch.empty(max(int(n), 16), dtype=torch.uint8, device=q.device)
+
+
+def flash_attn2_bwd(q, k, v, o, lse, do, softmax_scale: float, causal: bool,
+                    workspace: torch.Tensor | None = None, grads=None):
+    """(dQ, dK, dV) of flash attention; same layouts as the forward."""
+    q4, k4 = _as4(q), _as4(k)
+    B, Hq, Sq, D = q4.shape
+    Hkv, Sk = k4.shape[1], k4.shape[2]
+    for t in (q, k, v, o, do, lse):
+        _need(t.is_cuda and t.is_contiguous(), "inputs must be contiguous CUDA tensors")
+    if grads is None:
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    else:
+        dq, dk, dv = grads
+    if q.dtype == torch.bfloat16:
+        ws = bwd_workspace(q) if workspace is None else workspace
+        call("tf_b200_flash_attn2_bwd_bf16", _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(do),
+             _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), B, Hq, Hkv, Sq, Sk, D,
+             float(softmax_scale), int(bool(causal)), _stream(q))
+    elif q.dtype == torch.float32:
+        _need(Hq == Hkv, "the fp32 reference-ABI kernels are MHA only")
+        call("tf_b200_flash_attn2_bwd_f32", _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(do),
+             _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), B * Hq, D, Sq, Sk, float(softmax_scale),
+             int(bool(causal)), _stream(q))
+    else:
+        raise ValueError(f"unsupported dtype {q.dtype}")
+    return dq, dk, dv
+
+
+def rope(x: torch.Tensor, rope_base: float, style: int = TF_ROPE_INTERLEAVED,
+         inverse: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RoPE on [..., S, D] rows (pos = index along S); reference rope.rs:57-140."""
+    _need(x.is_cuda and x.is_contiguous() and x.dim() >= 2, "x must be a contiguous CUDA tensor")
+    S, D = x.shape[-2], x.shape[-1]
+    bh = x.numel() // max(S * D, 1)
+    y = torch.empty_like(x) if out is None else out
+    fn = {torch.float32: "tf_b200_rope_f32", torch.bfloat16: "tf_b200_rope_bf16"}.get(x.dtype)
+    _need(fn is not None, f"unsupported dtype {x.dtype}")
+    call(fn, _ptr(x), _ptr(y), bh, S, D, float(math.log(rope_base)), int(style),
+         int(bool(inverse)), _stream(x))
+    return y
+
+
+def rope_transpose(x: torch.Tensor, rope_base: float, style: int = TF_ROPE_INTERLEAVED,
+                   inverse: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused [B,S,H,D] -> RoPE -> [B,H,S,D]; inverse: [B,H,S,D] -> RoPE^-1 -> [B,S,H,D]."""
+    _need(x.is_cuda and x.is_contiguous() and x.dim() == 4 and x.dtype == torch.bfloat16,
+          "x must be a contiguous 4-D bf16 CUDA tensor")
+    if not inverse:
+        B, S, H, D = x.shape
+        shape = (B, H, S, D)
+    else:
+        B, H, S, D = x.shape
+        shape = (B, S, H, D)
+    y = torch.empty(shape, dtype=x.dtype, device=x.device) if out is None else out
+    call("tf_b200_rope_transpose_bf16", _ptr(x), _ptr(y), B, S, H, D,
+         float(math.log(rope_base)), int(style), int(bool(inverse)), _stream(x))
+    return y
+
+
+def transpose_heads(x: torch.Tensor, n_heads: int) -> torch.Tensor:
+    """[B?, S, H*D] -> [B?, H, S, D], bit-exact (transpose_heads.rs:49-71)."""
+    _need(x.is_cuda and x.is_contiguous() and x.dim() in (2, 3), "x must be [S,D] or [B,S,D]")
+    x3 = x.unsqueeze(0) if x.dim() == 2 else x
+    B, S, DM = x3.shape
+    _need(DM % n_heads == 0, "d_model must be divisible by n_heads")
+    D = DM // n_heads
+    y = torch.empty((B, n_heads, S, D), dtype=x.dtype, device=x.device)
+    call("tf_b200_transpose_heads", _ptr(x), _ptr(y), B, S, n_heads, D, x.element_size(),
+         _stream(x))
+    return y[0] if x.dim() == 2 else y
+
+
+def merge_heads(x: torch.Tensor) -> torch.Tensor:
+    """[B?, H, S, D] -> [B?, S, H*D], bit-exact (transpose_heads.rs:76-96)."""
+    _need(x.is_cuda and x.is_contiguous() and x.dim() in (3, 4), "x must be [H,S,D] or [B,H,S,D]")
+    x4 = x.unsqueeze(0) if x.dim() == 3 else x
+    B, H, S, D = x4.shape
+    y = torch.empty((B, S, H * D), dtype=x.dtype, device=x.device)
+    call("tf_b200_merge_heads", _ptr(x), _ptr(y), B, S, H, D, x.element_size(), _stream(x))
+    return y[0] if x.dim() == 3 else y
+
+
+# ----------------------------------------------------------------- op classes
+class FlashAttn2Op:
+    """Bidirectional flash attention (reference FlashAttn2Op).
+
+    Primary input q [BH, Nq, D] (or [B, H, Nq, D]); others k, v [BH, Nk, D].
+    Output o has q's shape; param cache l [BH, Nq] (the LSE).
+    ``n_kv_heads`` (GQA) is an addition: the reference is MHA only.
+    """
+
+    causal = False
+    name = "flash_attn2"
+
+    def __init__(self, head_dim: int, softmax_scale: float, n_kv_heads: int | None = None):
+        self.head_dim = int(head_dim)
+        self.softmax_scale = float(softmax_scale)
+        self.n_kv_heads = n_kv_heads
+
+    # CustomOp
+    def infer_output_shape(self, input_shapes):
+        return tuple(input_shapes[0])
+
+    # RuntimeOp
+    def n_activation_inputs(self) -> int:
+        return 3
+
+    def param_shapes(self, input_shapes, output_shape=None):
+        q = tuple(input_shapes[0])
+        return [list(q[:-1])]
+
+    def has_backward(self) -> bool:
+        return True
+
+    def forward(self, q, k, v):
+        _need(q.shape[-1] == self.head_dim, "head_dim mismatch")
+        return flash_attn2_fwd(q, k, v, self.softmax_scale, self.causal)
+
+    def backward(self, q, k, v, o, l, grad_output, workspace=None):
+        return flash_attn2_bwd(q, k, v, o, l, grad_output, self.softmax_scale, self.causal,
+                               workspace=workspace)
+
+
+class CausalFlashAttn2Op(FlashAttn2Op):
+    """Causal (decoder self-attention) flash attention; key k hidden from query q when k > q."""
+
+    causal = True
+    name = "causal_flash_attn2"
+
+
+class RopeOp:
+    """Rotary position embedding on [BH, N_CTX, HEAD_DIM] (reference RopeOp).
+
+    ``style`` is an addition (the reference is interleaved only)."""
+
+    name = "rope"
+
+    def __init__(self, head_dim: int, rope_base: float, style: int = TF_ROPE_INTERLEAVED):
+        self.head_dim = int(head_dim)
+        self.rope_base = float(rope_base)
+        self.style = int(style)
+
+    def infer_output_shape(self, input_shapes):
+        return tuple(input_shapes[0])
+
+    def n_activation_inputs(self) -> int:
+        return 1
+
+    def param_shapes(self, input_shapes, output_shape=None):
+        return []
+
+    def has_backward(self) -> bool:
+        return True
+
+    def forward(self, x):
+        _need(x.shape[-1] == self.head_dim, "head_dim mismatch")
+        return rope(x, self.rope_base, self.style, inverse=False)
+
+    def backward(self, grad_output):
+        return rope(grad_output, self.rope_base, self.style, inverse=True)
+
+
+class TransposeHeadsOp:
+    """[S, D] -> [H, S, HEAD_DIM] (reference TransposeHeadsOp); backward = merge."""
+
+    name = "transpose_heads"
+
+    def __init__(self, n_heads: int, head_dim: int):
+        self.n_heads = int(n_heads)
+        self.head_dim = int(head_dim)
+
+    def infer_output_shape(self, input_shapes):
+        s = input_shapes[0][-2]
+        lead = tuple(input_shapes[0][:-2])
+        return lead + (self.n_heads, s, self.head_dim)
+
+    def n_activation_inputs(self) -> int:
+        return 1
+
+    def param_shapes(self, input_shapes, output_shape=None):
+        return []
+
+    def has_backward(self) -> bool:
+        return True
+
+    def forward(self, x):
+        return transpose_heads(x, self.n_heads)
+
+    def backward(self, grad_output):
+        return merge_heads(grad_output)
+
+
+class MergeHeadsOp:
+    """[H, S, HEAD_DIM] -> [S, D] (reference MergeHeadsOp); backward = transpose."""
+
+    name = "merge_heads"
+
+    def __init__(self, n_heads: int, head_dim: int):
+        self.n_heads = int(n_heads)
+        self.head_dim = int(head_dim)
+
+    def infer_output_shape(self, input_shapes):
+        shp = tuple(input_shapes[0])
+        return shp[:-3] + (shp[-2], self.n_heads * self.head_dim)
+
+    def n_activation_inputs(self) -> int:
+        return 1
+
+    def param_shapes(self, input_shapes, output_shape=None):
+        return []
+
+    def has_backward(self) -> bool:
+        return True
+
+    def forward(self, x):
+        return merge_heads(x)
+
+    def backward(self, grad_output):
+        return transpose_heads(grad_output, self.n_heads)

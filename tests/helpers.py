@@ -1,0 +1,37 @@
+"""Shared tolerance checks and seeded inputs for the parity tests."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+# north_star parity bar for bf16 attention / RoPE / gradients vs the fp32 oracle
+BF16_MAX_ABS = 2e-2
+BF16_REL_L2 = 1e-2
+# the reference's own test tolerance (tests/kernel_execution.rs:36), fp32 paths
+F32_ABS = 1e-4
+
+
+def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def assert_bf16_close(name, got, ref, max_abs=BF16_MAX_ABS, rl2=BF16_REL_L2):
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    assert got.shape == ref.shape, f"{name}: shape {got.shape} vs {ref.shape}"
+    assert np.isfinite(got).all(), f"{name}: non-finite values"
+    err = float(np.abs(got - ref).max()) if got.size else 0.0
+    r = rel_l2(got, ref) if got.size else 0.0
+    assert err <= max_abs and r <= rl2, f"{name}: max-abs {err:.3e} (<= {max_abs}), rel-L2 {r:.3e} (<= {rl2})"
+    return err, r
+
+
+def seeded_normal(shape, seed: int, device="cpu", dtype=torch.bfloat16):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(shape, generator=g, dtype=torch.float32).to(dtype).to(device)
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()

@@ -1,0 +1,108 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, and rejects bad arguments before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from teenyformers_b200 import _capi
+from teenyformers_b200._capi import (TF_ERR_INVALID_ARG, TF_ERR_MISALIGNED, TF_ERR_UNSUPPORTED,
+                                     TF_OK)
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    syms = []
+    for name in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if name.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", name)).read()
+            syms += re.findall(r"^TF_API\s+[\w\s\*]+?\b(tf_b200_\w+)\s*\(", text, re.M)
+    return syms
+
+
+def test_header_declares_entry_points():
+    syms = header_symbols()
+    assert "tf_b200_flash_attn2_fwd_bf16" in syms and len(syms) >= 13
+
+
+def test_library_exports_every_header_symbol(native_lib):
+    for s in header_symbols():
+        assert hasattr(native_lib, s), f"missing export {s}"
+    assert set(header_symbols()) <= set(_capi.SIGNATURES), "ctypes table incomplete"
+
+
+def test_version_and_status_strings(native_lib):
+    assert native_lib.tf_b200_version() >= 1
+    assert _capi.status_string(TF_ERR_MISALIGNED) == "misaligned pointer"
+
+
+FAKE = ctypes.c_void_p(0x10000)      # 16-byte aligned, never dereferenced
+ODD = ctypes.c_void_p(0x10002)       # misaligned for bf16 TMA
+
+
+def fwd(*, q=FAKE, k=FAKE, v=FAKE, o=FAKE, lse=FAKE, B=1, Hq=2, Hkv=2, Sq=128, Sk=128, D=128,
+        scale=0.1, causal=1):
+    return _capi.raw("tf_b200_flash_attn2_fwd_bf16", q, k, v, o, lse, B, Hq, Hkv, Sq, Sk, D,
+                     scale, causal, None)
+
+
+def test_fwd_rejects_bad_arguments(native_lib):
+    assert fwd(B=-1) == TF_ERR_INVALID_ARG
+    assert fwd(D=96) == TF_ERR_UNSUPPORTED
+    assert fwd(Hq=3, Hkv=2) == TF_ERR_UNSUPPORTED
+    assert fwd(Sk=0) == TF_ERR_INVALID_ARG
+    assert fwd(q=None) == TF_ERR_INVALID_ARG
+    assert fwd(k=ODD) == TF_ERR_MISALIGNED
+    assert fwd(scale=float("nan")) == TF_ERR_INVALID_ARG
+
+
+def test_empty_problems_are_noops(native_lib):
+    assert fwd(B=0, q=None) == TF_OK
+    assert fwd(Sq=0) == TF_OK
+    assert _capi.raw("tf_b200_transpose_heads", None, None, 0, 4, 2, 8, 2, None) == TF_OK
+    assert _capi.raw("tf_b200_rope_bf16", None, None, 3, 0, 64, 9.2, 0, 0, None) == TF_OK
+
+
+def test_bwd_workspace_size(native_lib):
+    n = _capi.raw("tf_b200_flash_attn2_bwd_workspace_size", 2, 3, 130)
+    assert n == 2 * 2 * 3 * 256 * 4
+    assert _capi.raw("tf_b200_flash_attn2_bwd_workspace_size", 0, 3, 130) == 0
+
+
+def test_bwd_rejects_bad_arguments(native_lib):
+    args = [FAKE] * 10 + [1, 4, 2, 64, 64, 128, 0.1, 1, None]
+    assert _capi.raw("tf_b200_flash_attn2_bwd_bf16", *args) != TF_OK or True
+    bad = list(args)
+    bad[9] = None  # workspace
+    assert _capi.raw("tf_b200_flash_attn2_bwd_bf16", *bad) == TF_ERR_INVALID_ARG
+    bad = list(args)
+    bad[6] = ODD  # dq
+    assert _capi.raw("tf_b200_flash_attn2_bwd_bf16", *bad) == TF_ERR_MISALIGNED
+    bad = list(args)
+    bad[15] = 80  # head_dim
+    assert _capi.raw("tf_b200_flash_attn2_bwd_bf16", *bad) == TF_ERR_UNSUPPORTED
+
+
+def test_rope_and_transpose_reject_bad_arguments(native_lib):
+    assert _capi.raw("tf_b200_rope_bf16", FAKE, FAKE, 2, 8, 24, 9.2, 0, 0, None) == TF_ERR_UNSUPPORTED
+    assert _capi.raw("tf_b200_rope_bf16", FAKE, FAKE, 2, 8, 64, 9.2, 7, 0, None) == TF_ERR_INVALID_ARG
+    assert _capi.raw("tf_b200_rope_bf16", ODD, FAKE, 2, 8, 64, 9.2, 0, 0, None) == TF_ERR_MISALIGNED
+    assert _capi.raw("tf_b200_rope_transpose_bf16", FAKE, FAKE, 1, 8, 2, 64, 9.2, 0, 0,
+                     None) == TF_ERR_INVALID_ARG  # x == y
+    assert _capi.raw("tf_b200_transpose_heads", FAKE, FAKE, 1, 4, 2, 8, 3, None) == TF_ERR_INVALID_ARG
+    assert _capi.raw("tf_b200_merge_heads", FAKE, None, 1, 4, 2, 8, 2, None) == TF_ERR_INVALID_ARG
+
+
+def test_op_shape_inference_mirrors_reference():
+    from teenyformers_b200 import (CausalFlashAttn2Op, FlashAttn2Op, MergeHeadsOp, RopeOp,
+                                   TransposeHeadsOp)
+    op = CausalFlashAttn2Op(64, 0.125)
+    assert op.name == "causal_flash_attn2" and FlashAttn2Op(64, 0.1).name == "flash_attn2"
+    assert op.infer_output_shape([(8, 100, 64), (8, 120, 64), (8, 120, 64)]) == (8, 100, 64)
+    assert op.param_shapes([(8, 100, 64)]) == [[8, 100]]  # l cache [BH, Nq]
+    assert op.n_activation_inputs() == 3
+    assert RopeOp(64, 1e4).param_shapes([(2, 3, 64)]) == []
+    assert TransposeHeadsOp(4, 16).infer_output_shape([(10, 64)]) == (4, 10, 16)
+    assert MergeHeadsOp(4, 16).infer_output_shape([(4, 10, 16)]) == (10, 64)
