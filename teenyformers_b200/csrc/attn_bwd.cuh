@@ -16,12 +16,19 @@
 //     their P is exactly 0).
 //  2. fa_bwd_dkdv_sm100_kernel: one CTA per 128-key tile of one KV head,
 //     looping over the 128-row query tiles of every query head of the GQA
-//     group.  TMEM: S^T [0,128), dP^T [128,256), dV [256,256+D),
-//     dK [256+D, 256+2D).  P^T and dS^T (bf16) overwrite the first 64
-//     columns of S^T / dP^T and feed dV += P^T dO, dK += dS^T Q straight
-//     from TMEM.
+//     group.  Each query tile is processed as two 64-query halves h so the
+//     elementwise work on one half overlaps the MMAs of the other:
+//       S^T_h = K Q_h^T, dP^T_h = V dO_h^T        (M=128 keys, N=64)
+//       P^T_h, dS^T_h in bf16 over the first 32 columns of S^T_h / dP^T_h
+//       dV += P^T_h dO_h, dK += dS^T_h Q_h         (A from TMEM, K=64)
+//     TMEM: S^T_0 [0,64) S^T_1 [64,128) dP^T_0 [128,192) dP^T_1 [192,256)
+//           dV [256,256+D) dK [256+D,256+2D).
+//     S^T_0/dP^T_0 of the next query tile are issued as soon as the dV/dK
+//     MMAs of half 0 are queued (tcgen05 MMAs of one thread run in order).
 //  3. fa_bwd_dq_sm100_kernel: one CTA per 128-row query tile, looping over
-//     key tiles: S, dP in TMEM, dS (bf16) over S, dQ += dS K.
+//     key tiles in two 64-key halves: S_h = Q K_h^T, dP_h = dO V_h^T,
+//     dS_h (bf16) over S_h, dQ += dS_h K_h.  TMEM: S_0 S_1 dP_0 dP_1 as
+//     above, dQ [256,256+D).
 // Roles: warps 0-3 elementwise (one TMEM lane = one row per thread),
 // warp 4 MMA issuer, warp 5 TMA producer.
 #pragma once
@@ -98,8 +105,7 @@ __device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, ui
 }
 
 __device__ __forceinline__ void mbar_wait_noabort(uint32_t bar, uint32_t parity, int site) {
-  int dummy = 0;
-  (void)mbar_wait(bar, parity, (volatile int*)&dummy, site);
+  (void)mbar_wait(bar, parity, nullptr, site);
 }
 
 template <int D>
@@ -118,8 +124,10 @@ struct BwdKvCfg {
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES + 1024;
   static constexpr int OFF_BAR = OFF_STAGE + 2 * STAGE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
-  static constexpr uint32_t TM_ST = 0, TM_DPT = 128, TM_DV = 256, TM_DK = 256 + D;
+  static constexpr uint32_t TM_DV = 256, TM_DK = 256 + D;
   static constexpr uint32_t TM_COLS = 512;
+  __device__ static constexpr uint32_t tm_st(int h) { return uint32_t(h) * 64u; }
+  __device__ static constexpr uint32_t tm_dpt(int h) { return 128u + uint32_t(h) * 64u; }
 };
 
 template <int D>
@@ -134,14 +142,16 @@ struct BwdQCfg {
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_STAGE + 2 * STAGE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
-  static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DQ = 256;
+  static constexpr uint32_t TM_DQ = 256;
   static constexpr uint32_t TM_COLS = 512;
+  __device__ static constexpr uint32_t tm_s(int h) { return uint32_t(h) * 64u; }
+  __device__ static constexpr uint32_t tm_dp(int h) { return 128u + uint32_t(h) * 64u; }
 };
 
-enum BwdKvBar { KB_KV = 0, KB_QFULL = 1, KB_QEMPTY = 3, KB_SFULL = 5, KB_PFULL = 6,
-                KB_ACC = 7, KB_DRAIN = 8, KB_COUNT = 9 };
-enum BwdQBar { QB_Q = 0, QB_KVFULL = 1, QB_KVEMPTY = 3, QB_SFULL = 5, QB_PFULL = 6,
-               QB_ACC = 7, QB_DRAIN = 8, QB_COUNT = 9 };
+enum BwdKvBar { KB_KV = 0, KB_QFULL = 1, KB_QEMPTY = 3, KB_SFULL = 5, KB_PFULL = 7,
+                KB_ACC = 9, KB_DRAIN = 10, KB_COUNT = 11 };
+enum BwdQBar { QB_Q = 0, QB_KVFULL = 1, QB_KVEMPTY = 3, QB_SFULL = 5, QB_PFULL = 7,
+               QB_ACC = 9, QB_DRAIN = 10, QB_COUNT = 11 };
 
 // Stores one 32-column fp32 TMEM chunk (scaled) as 32 bf16 to global.
 __device__ __forceinline__ void store_row_chunk_bf16(__nv_bfloat16* dst, const uint32_t (&r)[32],
@@ -153,6 +163,22 @@ __device__ __forceinline__ void store_row_chunk_bf16(__nv_bfloat16* dst, const u
   uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
   for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+}
+
+// Operand descriptors are built once per buffer and advanced per step by a
+// compile-time constant (desc_adv).  A 128-row tile is stored as D/64
+// column halves of 128 rows x 128 bytes (SW128):
+//  - read K-major (rows = M or N, 64-element atoms along K):  base LBO 16,
+//    step kk at kstep_off(kk), 64-row sub-tile row0 at + row0 * 128;
+//  - read MN-major as K x N with N = D (rows = K): base LBO = HALF_BYTES,
+//    K rows row0 + 16 kk at + (row0 + 16 kk) * 128.
+template <int HALF_BYTES>
+__device__ __forceinline__ uint64_t kmajor_base(uint32_t tile) {
+  return make_sdesc_sw128(tile, 16, 1024);
+}
+template <int HALF_BYTES>
+__device__ __forceinline__ uint64_t mnmajor_base(uint32_t tile) {
+  return make_sdesc_sw128(tile, HALF_BYTES, 1024);
 }
 
 // ------------------------------------------------------------------ dK / dV
@@ -188,9 +214,9 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(KB_QFULL + s), 1);
       mbar_init(bar(KB_QEMPTY + s), 1);
+      mbar_init(bar(KB_SFULL + s), 1);
+      mbar_init(bar(KB_PFULL + s), 128);
     }
-    mbar_init(bar(KB_SFULL), 1);
-    mbar_init(bar(KB_PFULL), 128);
     mbar_init(bar(KB_ACC), 1);
     mbar_init(bar(KB_DRAIN), 1);
     *abort_flag = 0;
@@ -208,7 +234,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 5) {
     // ---------------- TMA producer ----------------
     if (lane == 0 && n_tiles > 0) {
-      int issued[2] = {0, 0};
+      int issued0 = 0, issued1 = 0;
       bool ok = true;
       mbar_arrive_expect_tx(bar(KB_KV), 2 * C::TILE_BYTES);
       for (int hh = 0; hh < C::HALVES; ++hh) {
@@ -233,59 +259,89 @@ __global__ void __launch_bounds__(192, 1)
         const size_t ws_off = (size_t)bh_q * p.Sq_pad + (size_t)qi * 128;
         bulk_load(sb + C::STAGE_LSE, p.ws_lse2 + ws_off, 512, bar(KB_QFULL + st));
         bulk_load(sb + C::STAGE_DELTA, p.ws_delta + ws_off, 512, bar(KB_QFULL + st));
-        ++issued[st];
+        (st ? issued1 : issued0) += 1;
       }
       if (!ok) {
         mbar_wait_noabort(bar(KB_KV), 0, 402);
-        for (int s = 0; s < 2; ++s)
-          if (issued[s]) mbar_wait_noabort(bar(KB_QFULL + s), (issued[s] - 1) & 1, 402);
+        if (issued0) mbar_wait_noabort(bar(KB_QFULL + 0), (issued0 - 1) & 1, 402);
+        if (issued1) mbar_wait_noabort(bar(KB_QFULL + 1), (issued1 - 1) & 1, 402);
       }
     }
   } else if (warp == 4) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && n_tiles > 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
       constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);
+      const uint64_t d_k = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_K);
+      const uint64_t d_v = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_V);
+      const uint64_t d_q0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::STAGE_Q);
+      const uint64_t d_do0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::STAGE_DO);
+      const uint64_t m_q0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::STAGE_Q);
+      const uint64_t m_do0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::STAGE_DO);
+      // S^T_h = K Q_h^T and dP^T_h = V dO_h^T for stage st
+      auto issue_s = [&](int h, int st) {
+        const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
+        const uint64_t bq = desc_adv(d_q0, so), bdo = desc_adv(d_do0, so);
+        const uint32_t dst = tmem + C::tm_st(h), ddp = tmem + C::tm_dpt(h);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(dst, desc_adv(d_k, kstep_off(kk, C::HALF_BYTES)),
+                 desc_adv(bq, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(ddp, desc_adv(d_v, kstep_off(kk, C::HALF_BYTES)),
+                 desc_adv(bdo, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+      };
+      // dV += P^T_h dO_h, dK += dS^T_h Q_h
+      auto issue_acc = [&](int h, int st, bool acc) {
+        const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
+        const uint64_t bdo = desc_adv(m_do0, so), bq = desc_adv(m_q0, so);
+        const uint32_t ap = tmem + C::tm_st(h), ads = tmem + C::tm_dpt(h);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ts(tmem + C::TM_DV, ap + kk * 8, desc_adv(bdo, kk * 16 * 128), idesc_acc,
+                 (acc || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ts(tmem + C::TM_DK, ads + kk * 8, desc_adv(bq, kk * 16 * 128), idesc_acc,
+                 (acc || kk > 0) ? 1u : 0u);
+      };
       bool ok = mbar_wait(bar(KB_KV), 0, abort_flag, 411);
+      if (ok) ok = mbar_wait(bar(KB_QFULL + 0), 0, abort_flag, 412);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        tc_commit(bar(KB_SFULL + 0));
+        issue_s(1, 0);
+        tc_commit(bar(KB_SFULL + 1));
+      }
       for (int it = 0; it < n_tiles && ok; ++it) {
         const int st = it & 1;
-        ok = mbar_wait(bar(KB_QFULL + st), (it >> 1) & 1, abort_flag, 412);
+        const bool more = it + 1 < n_tiles;
+        ok = mbar_wait(bar(KB_PFULL + 0), it & 1, abort_flag, 413);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + C::TM_ST, make_sdesc_sw128(sbase + C::OFF_K + off, 16, 1024),
-                 make_sdesc_sw128(sb + C::STAGE_Q + off, 16, 1024), idesc_s, kk > 0);
+        issue_acc(0, st, it > 0);
+        if (more) {
+          ok = mbar_wait(bar(KB_QFULL + (st ^ 1)), ((it + 1) >> 1) & 1, abort_flag, 414);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(0, st ^ 1);
+          tc_commit(bar(KB_SFULL + 0));
         }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + C::TM_DPT, make_sdesc_sw128(sbase + C::OFF_V + off, 16, 1024),
-                 make_sdesc_sw128(sb + C::STAGE_DO + off, 16, 1024), idesc_s, kk > 0);
-        }
-        tc_commit(bar(KB_SFULL));
-        ok = mbar_wait(bar(KB_PFULL), it & 1, abort_flag, 413);
+        ok = mbar_wait(bar(KB_PFULL + 1), it & 1, abort_flag, 415);
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          mma_ts(tmem + C::TM_DV, tmem + C::TM_ST + kk * 8,
-                 make_sdesc_sw128(sb + C::STAGE_DO + kk * 2048, C::HALF_BYTES, 1024), idesc_acc,
-                 (it > 0 || kk > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          mma_ts(tmem + C::TM_DK, tmem + C::TM_DPT + kk * 8,
-                 make_sdesc_sw128(sb + C::STAGE_Q + kk * 2048, C::HALF_BYTES, 1024), idesc_acc,
-                 (it > 0 || kk > 0) ? 1u : 0u);
-        }
+        issue_acc(1, st, true);
         tc_commit(bar(KB_QEMPTY + st));
+        if (more) {
+          issue_s(1, st ^ 1);
+          tc_commit(bar(KB_SFULL + 1));
+        }
       }
       if (ok) tc_commit(bar(KB_ACC));
       tc_commit(bar(KB_DRAIN));
-      mbar_wait_noabort(bar(KB_DRAIN), 0, 414);
+      mbar_wait_noabort(bar(KB_DRAIN), 0, 416);
     }
   } else {
     // ---------------- elementwise: warps 0-3, thread = key row ----------------
@@ -297,43 +353,53 @@ __global__ void __launch_bounds__(192, 1)
     for (int it = 0; it < n_tiles && ok; ++it) {
       const int st = it & 1;
       const int qi = qt_first + it % qt_per_head;
-      ok = mbar_wait(bar(KB_SFULL), it & 1, abort_flag, 421);
-      if (ok) ok = mbar_wait(bar(KB_QFULL + st), (it >> 1) & 1, abort_flag, 422);
-      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
-      if (!ok) break;
-      tc_fence_after();
       const uint8_t* sb = smem + C::OFF_STAGE + st * C::STAGE_BYTES;
-      const float* s_lse = reinterpret_cast<const float*>(sb + C::STAGE_LSE);
-      const float* s_delta = reinterpret_cast<const float*>(sb + C::STAGE_DELTA);
+      const float4* s_lse = reinterpret_cast<const float4*>(sb + C::STAGE_LSE);
+      const float4* s_delta = reinterpret_cast<const float4*>(sb + C::STAGE_DELTA);
       const bool diag = p.causal && qi * 128 < k0 + 127;
-      const int qlim = key - qi * 128;  // columns with index < qlim are hidden (k > q)
+      const int qlim = key - qi * 128;  // query columns with index < qlim are hidden (k > q)
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + C::TM_ST + c * 32, sr);
-        tmem_ld32(tmem + lane_base + C::TM_DPT + c * 32, dr);
-        tmem_wait_ld();
-        uint32_t pk[16], dk[16];
+      for (int h = 0; h < 2 && ok; ++h) {
+        ok = mbar_wait(bar(KB_SFULL + h), it & 1, abort_flag, 421);
+        if (ok && h == 0) ok = mbar_wait(bar(KB_QFULL + st), (it >> 1) & 1, abort_flag, 422);
+        ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          const int col0 = h * 64 + c * 32;  // query column of this chunk within the tile
+          uint32_t sr[32], dr[32];
+          tmem_ld32(tmem + lane_base + C::tm_st(h) + c * 32, sr);
+          tmem_ld32(tmem + lane_base + C::tm_dpt(h) + c * 32, dr);
+          tmem_wait_ld();
+          uint32_t pk[16], dk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c0 = c * 32 + 2 * i;
-          float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -s_lse[c0]));
-          float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -s_lse[c0 + 1]));
-          if (diag) {
-            if (c0 < qlim) p0 = 0.0f;
-            if (c0 + 1 < qlim) p1 = 0.0f;
+          for (int v4 = 0; v4 < 8; ++v4) {
+            const float4 l4 = s_lse[col0 / 4 + v4];
+            const float4 d4 = s_delta[col0 / 4 + v4];
+            const float lq[4] = {l4.x, l4.y, l4.z, l4.w};
+            const float dq[4] = {d4.x, d4.y, d4.z, d4.w};
+            float pv[4], dsv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = v4 * 4 + e;
+              float pe = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, -lq[e]));
+              if (diag && col0 + i < qlim) pe = 0.0f;
+              pv[e] = pe;
+              dsv[e] = pe * (__uint_as_float(dr[i]) - dq[e]);
+            }
+            pk[2 * v4] = pack_bf16x2(pv[0], pv[1]);
+            pk[2 * v4 + 1] = pack_bf16x2(pv[2], pv[3]);
+            dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
+            dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
           }
-          const float d0 = p0 * (__uint_as_float(dr[2 * i]) - s_delta[c0]);
-          const float d1 = p1 * (__uint_as_float(dr[2 * i + 1]) - s_delta[c0 + 1]);
-          pk[i] = pack_bf16x2(p0, p1);
-          dk[i] = pack_bf16x2(d0, d1);
+          tmem_st16(tmem + lane_base + C::tm_st(h) + c * 16, pk);
+          tmem_st16(tmem + lane_base + C::tm_dpt(h) + c * 16, dk);
         }
-        tmem_st16(tmem + lane_base + C::TM_ST + c * 16, pk);
-        tmem_st16(tmem + lane_base + C::TM_DPT + c * 16, dk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(KB_PFULL + h));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(KB_PFULL));
     }
     // ---- epilogue: dV = acc, dK = acc * scale ----
     const bool valid = key < p.Sk;
@@ -386,11 +452,12 @@ __global__ void __launch_bounds__(192, 1)
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  int qi = blockIdx.x / p.BHq;
-  const int bh = blockIdx.x % p.BHq;
-  if (p.causal) qi = p.n_qt - 1 - qi;  // heavy first
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
+  // Head-major (K/V of a head stay hot in L2), heavy query tiles first.
+  const int bh = blockIdx.x / p.n_qt;
+  int qi = blockIdx.x % p.n_qt;
+  if (p.causal) qi = p.n_qt - 1 - qi;
+  const int b = bh / p.Hq, h_q = bh % p.Hq;
+  const int bh_kv = b * p.Hkv + h_q / (p.Hq / p.Hkv);
   const int q0 = qi * 128;
   int n_kv = p.n_kt;
   if (p.causal) n_kv = min(p.n_kt, (min(p.Sq, q0 + 128) - 1) / 128 + 1);
@@ -400,9 +467,9 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(QB_KVFULL + s), 1);
       mbar_init(bar(QB_KVEMPTY + s), 1);
+      mbar_init(bar(QB_SFULL + s), 1);
+      mbar_init(bar(QB_PFULL + s), 128);
     }
-    mbar_init(bar(QB_SFULL), 1);
-    mbar_init(bar(QB_PFULL), 128);
     mbar_init(bar(QB_ACC), 1);
     mbar_init(bar(QB_DRAIN), 1);
     *abort_flag = 0;
@@ -419,7 +486,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 5) {
     if (lane == 0) {
-      int issued[2] = {0, 0};
+      int issued0 = 0, issued1 = 0;
       bool ok = true;
       mbar_arrive_expect_tx(bar(QB_Q), 2 * C::TILE_BYTES);
       for (int hh = 0; hh < C::HALVES; ++hh) {
@@ -438,53 +505,82 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_3d(sb + C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v, bar(QB_KVFULL + st),
                       hh * 64, j * 128, bh_kv);
         }
-        ++issued[st];
+        (st ? issued1 : issued0) += 1;
       }
       if (!ok) {
         mbar_wait_noabort(bar(QB_Q), 0, 502);
-        for (int s = 0; s < 2; ++s)
-          if (issued[s]) mbar_wait_noabort(bar(QB_KVFULL + s), (issued[s] - 1) & 1, 502);
+        if (issued0) mbar_wait_noabort(bar(QB_KVFULL + 0), (issued0 - 1) & 1, 502);
+        if (issued1) mbar_wait_noabort(bar(QB_KVFULL + 1), (issued1 - 1) & 1, 502);
       }
     }
   } else if (warp == 4) {
     if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
       constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
+      const uint64_t d_q = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_Q);
+      const uint64_t d_do = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_DO);
+      const uint64_t d_k0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
+      const uint64_t d_v0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::TILE_BYTES);
+      const uint64_t m_k0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
+      // S_h = Q K_h^T, dP_h = dO V_h^T for key stage st
+      auto issue_s = [&](int h, int st) {
+        const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
+        const uint64_t bk = desc_adv(d_k0, so), bv = desc_adv(d_v0, so);
+        const uint32_t ds = tmem + C::tm_s(h), ddp = tmem + C::tm_dp(h);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(ds, desc_adv(d_q, kstep_off(kk, C::HALF_BYTES)),
+                 desc_adv(bk, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(ddp, desc_adv(d_do, kstep_off(kk, C::HALF_BYTES)),
+                 desc_adv(bv, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+      };
+      // dQ += dS_h K_h
+      auto issue_dq = [&](int h, int st, bool acc) {
+        const uint64_t bk = desc_adv(m_k0, st * C::STAGE_BYTES + h * 64 * 128);
+        const uint32_t a = tmem + C::tm_s(h);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ts(tmem + C::TM_DQ, a + kk * 8, desc_adv(bk, kk * 16 * 128), idesc_dq,
+                 (acc || kk > 0) ? 1u : 0u);
+      };
       bool ok = mbar_wait(bar(QB_Q), 0, abort_flag, 511);
+      if (ok) ok = mbar_wait(bar(QB_KVFULL + 0), 0, abort_flag, 512);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        tc_commit(bar(QB_SFULL + 0));
+        issue_s(1, 0);
+        tc_commit(bar(QB_SFULL + 1));
+      }
       for (int j = 0; j < n_kv && ok; ++j) {
         const int st = j & 1;
-        ok = mbar_wait(bar(QB_KVFULL + st), (j >> 1) & 1, abort_flag, 512);
+        const bool more = j + 1 < n_kv;
+        ok = mbar_wait(bar(QB_PFULL + 0), j & 1, abort_flag, 513);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t sk = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
-        const uint32_t sv = sk + C::TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + C::TM_S, make_sdesc_sw128(sbase + C::OFF_Q + off, 16, 1024),
-                 make_sdesc_sw128(sk + off, 16, 1024), idesc_s, kk > 0);
+        issue_dq(0, st, j > 0);
+        if (more) {
+          ok = mbar_wait(bar(QB_KVFULL + (st ^ 1)), ((j + 1) >> 1) & 1, abort_flag, 514);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(0, st ^ 1);
+          tc_commit(bar(QB_SFULL + 0));
         }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + C::TM_DP, make_sdesc_sw128(sbase + C::OFF_DO + off, 16, 1024),
-                 make_sdesc_sw128(sv + off, 16, 1024), idesc_s, kk > 0);
-        }
-        tc_commit(bar(QB_SFULL));
-        ok = mbar_wait(bar(QB_PFULL), j & 1, abort_flag, 513);
+        ok = mbar_wait(bar(QB_PFULL + 1), j & 1, abort_flag, 515);
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          mma_ts(tmem + C::TM_DQ, tmem + C::TM_S + kk * 8,
-                 make_sdesc_sw128(sk + kk * 2048, C::HALF_BYTES, 1024), idesc_dq,
-                 (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        issue_dq(1, st, true);
         tc_commit(bar(QB_KVEMPTY + st));
+        if (more) {
+          issue_s(1, st ^ 1);
+          tc_commit(bar(QB_SFULL + 1));
+        }
       }
       if (ok) tc_commit(bar(QB_ACC));
       tc_commit(bar(QB_DRAIN));
-      mbar_wait_noabort(bar(QB_DRAIN), 0, 514);
+      mbar_wait_noabort(bar(QB_DRAIN), 0, 516);
     }
   } else {
     const int row = warp * 32 + lane;
@@ -496,38 +592,41 @@ __global__ void __launch_bounds__(192, 1)
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
-      ok = mbar_wait(bar(QB_SFULL), j & 1, abort_flag, 521);
-      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
-      if (!ok) break;
-      tc_fence_after();
       const int kb = j * 128;
       const bool need_mask = (p.causal && kb + 127 > q0) || (kb + 128 > p.Sk);
-      int lim = p.Sk - 1 - kb;  // columns with index > lim are hidden
+      int lim = p.Sk - 1 - kb;  // key columns with index > lim are hidden
       if (p.causal) lim = min(lim, qrow - kb);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + C::TM_S + c * 32, sr);
-        tmem_ld32(tmem + lane_base + C::TM_DP + c * 32, dr);
-        tmem_wait_ld();
-        uint32_t dsk[16];
+      for (int h = 0; h < 2 && ok; ++h) {
+        ok = mbar_wait(bar(QB_SFULL + h), j & 1, abort_flag, 521);
+        ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          const int col0 = h * 64 + c * 32;
+          uint32_t sr[32], dr[32];
+          tmem_ld32(tmem + lane_base + C::tm_s(h) + c * 32, sr);
+          tmem_ld32(tmem + lane_base + C::tm_dp(h) + c * 32, dr);
+          tmem_wait_ld();
+          uint32_t dsk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c0 = c * 32 + 2 * i;
-          float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -lse2));
-          float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -lse2));
-          if (need_mask) {
-            if (c0 > lim) p0 = 0.0f;
-            if (c0 + 1 > lim) p1 = 0.0f;
+          for (int i = 0; i < 16; ++i) {
+            float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -lse2));
+            float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -lse2));
+            if (need_mask) {
+              if (col0 + 2 * i > lim) p0 = 0.0f;
+              if (col0 + 2 * i + 1 > lim) p1 = 0.0f;
+            }
+            dsk[i] = pack_bf16x2(p0 * (__uint_as_float(dr[2 * i]) - delta),
+                                 p1 * (__uint_as_float(dr[2 * i + 1]) - delta));
           }
-          dsk[i] = pack_bf16x2(p0 * (__uint_as_float(dr[2 * i]) - delta),
-                               p1 * (__uint_as_float(dr[2 * i + 1]) - delta));
+          tmem_st16(tmem + lane_base + C::tm_s(h) + c * 16, dsk);
         }
-        tmem_st16(tmem + lane_base + C::TM_S + c * 16, dsk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(QB_PFULL + h));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(QB_PFULL));
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(bar(QB_ACC), 0, abort_flag, 522))) {
       tc_fence_after();

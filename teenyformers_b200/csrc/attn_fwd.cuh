@@ -21,8 +21,13 @@
 //   S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
 // P_t (bf16 pairs) overwrites the first 64 columns of S_t; the next S_t MMA
 // is issued after the P_t V_j MMA, and tcgen05 MMAs of one thread execute in
-// issue order.  The running max is rescaled lazily: O and l are only
-// rescaled when the row max grows by more than 2^8 (P stays <= 256).
+// issue order.  P_t is handed to the MMA issuer in two 64-key halves (two
+// phases of one mbarrier per iteration) so the first half of P_t V_j runs
+// while the softmax finishes the second half.  The issuing thread blocks
+// while the tensor pipe's queue is full, so its bookkeeping (slot-release
+// commits) is deferred until the next batch of MMAs is queued.  The running
+// max is rescaled lazily: O and l are only rescaled when the row max grows
+// by more than 2^8 (P stays <= 256).
 // Every mbarrier wait is bounded (sm100.cuh); a timeout unwinds the CTA.
 #pragma once
 
@@ -65,17 +70,17 @@ enum FwdBar {
   FB_VFULL = 5,   // 2
   FB_VEMPTY = 7,  // 2
   FB_SFULL = 9,   // 2
-  FB_PFULL = 11,  // 2
+  FB_PFULL = 11,  // 2: keys 0..63 of P_t ready
   FB_ODONE = 13,  // 2
   FB_DRAIN = 15,
-  FB_COUNT = 16
+  FB_PFULL1 = 16,  // 2: keys 64..127 of P_t ready
+  FB_COUNT = 18
 };
 
 // Waits without looking at the abort flag (used to drain in-flight async
 // work before the CTA exits); bounded by kWaitTimeoutNs.
 __device__ __forceinline__ void mbar_drain_wait(uint32_t bar, uint32_t parity, int site) {
-  int dummy = 0;
-  (void)mbar_wait(bar, parity, (volatile int*)&dummy, site);
+  (void)mbar_wait(bar, parity, nullptr, site);
 }
 
 template <int D>
@@ -95,28 +100,24 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // ---- work decode: heavy (late) query-tile pairs first for causal ----
-  int pair = blockIdx.x / p.BHq;
-  const int bh = blockIdx.x % p.BHq;
+  // ---- work decode: head-major, so the CTAs resident at any time share a
+  // few heads' K/V in L2; within a head, heavy (late) pairs first for causal.
+  const int bh = blockIdx.x / p.n_pairs;
+  int pair = blockIdx.x % p.n_pairs;
   if (p.causal) pair = p.n_pairs - 1 - pair;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
   const int q0 = pair * 256;
   const int n_kv_all = (p.Sk + 127) / 128;
-  int nkv[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
+  auto tile_kv = [&](int t) {  // key tiles query tile t needs (0 if it is past Sq)
     const int qs = q0 + 128 * t;
-    if (qs >= p.Sq) {
-      nkv[t] = 0;
-    } else if (p.causal) {
-      const int last_q = min(p.Sq, qs + 128) - 1;
-      nkv[t] = min(n_kv_all, last_q / 128 + 1);
-    } else {
-      nkv[t] = n_kv_all;
-    }
-  }
-  const int n_iter = max(nkv[0], nkv[1]);
+    if (qs >= p.Sq) return 0;
+    if (!p.causal) return n_kv_all;
+    return min(n_kv_all, (min(p.Sq, qs + 128) - 1) / 128 + 1);
+  };
+  const int nkv0 = tile_kv(0), nkv1 = tile_kv(1);
+  auto nkv = [&](int t) { return t ? nkv1 : nkv0; };
+  const int n_iter = max(nkv0, nkv1);
 
   // ---- setup ----
   if (threadIdx.x == 0) {
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(FB_VEMPTY + s), 1);
       mbar_init(bar(FB_SFULL + s), 1);
       mbar_init(bar(FB_PFULL + s), 128);
+      mbar_init(bar(FB_PFULL1 + s), 128);
       mbar_init(bar(FB_ODONE + s), 1);
     }
     mbar_init(bar(FB_DRAIN), 1);
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 9) {
     // =================== TMA producer ===================
     if (lane == 0) {
-      int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};
+      int issued_k0 = 0, issued_k1 = 0, issued_v0 = 0, issued_v1 = 0;
       bool ok = true;
       mbar_arrive_expect_tx(bar(FB_QFULL), 2 * C::TILE_BYTES);
       for (int t = 0; t < 2; ++t)
@@ -166,22 +168,22 @@ __global__ void __launch_bounds__(320, 1)
         for (int hh = 0; hh < C::HALVES; ++hh)
           tma_load_3d(sbase + C::OFF_K + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_k,
                       bar(FB_KFULL + s), hh * 64, j * 128, bh_kv);
-        ++issued_k[s];
+        (s ? issued_k1 : issued_k0) += 1;
         if (u > 0) ok = mbar_wait(bar(FB_VEMPTY + s), (u - 1) & 1, abort_flag, 102);
         if (!ok) break;
         mbar_arrive_expect_tx(bar(FB_VFULL + s), C::TILE_BYTES);
         for (int hh = 0; hh < C::HALVES; ++hh)
           tma_load_3d(sbase + C::OFF_V + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v,
                       bar(FB_VFULL + s), hh * 64, j * 128, bh_kv);
-        ++issued_v[s];
+        (s ? issued_v1 : issued_v0) += 1;
       }
       if (!ok) {
         // Abort: let every issued copy land before the CTA's smem goes away.
         mbar_drain_wait(bar(FB_QFULL), 0, 103);
-        for (int s = 0; s < 2; ++s) {
-          if (issued_k[s]) mbar_drain_wait(bar(FB_KFULL + s), (issued_k[s] - 1) & 1, 103);
-          if (issued_v[s]) mbar_drain_wait(bar(FB_VFULL + s), (issued_v[s] - 1) & 1, 103);
-        }
+        if (issued_k0) mbar_drain_wait(bar(FB_KFULL + 0), (issued_k0 - 1) & 1, 103);
+        if (issued_k1) mbar_drain_wait(bar(FB_KFULL + 1), (issued_k1 - 1) & 1, 103);
+        if (issued_v0) mbar_drain_wait(bar(FB_VFULL + 0), (issued_v0 - 1) & 1, 103);
+        if (issued_v1) mbar_drain_wait(bar(FB_VFULL + 1), (issued_v1 - 1) & 1, 103);
       }
     }
   } else if (warp == 8) {
@@ -189,23 +191,32 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_bf16(128, D, 0, 1);
+      // Descriptors are built once; each K step only advances the start
+      // address by a compile-time constant.
+      const uint64_t dq0 = make_sdesc_sw128(sbase + C::OFF_Q, 16, 1024);
+      const uint64_t dq1 = desc_adv(dq0, C::TILE_BYTES);
+      const uint64_t dk0 = make_sdesc_sw128(sbase + C::OFF_K, 16, 1024);
+      const uint64_t dk1 = desc_adv(dk0, C::TILE_BYTES);
+      const uint64_t dv0 = make_sdesc_sw128(sbase + C::OFF_V, C::HALF_BYTES, 1024);
+      const uint64_t dv1 = desc_adv(dv0, C::TILE_BYTES);
       auto issue_qk = [&](int t, int slot) {
-        const uint32_t a0 = sbase + C::OFF_Q + t * C::TILE_BYTES;
-        const uint32_t b0 = sbase + C::OFF_K + slot * C::TILE_BYTES;
+        const uint64_t a = t ? dq1 : dq0;
+        const uint64_t bk = slot ? dk1 : dk0;
+        const uint32_t d = tmem + C::tm_s(t);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::HALF_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + C::tm_s(t), make_sdesc_sw128(a0 + off, 16, 1024),
-                 make_sdesc_sw128(b0 + off, 16, 1024), idesc_qk, kk > 0);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(d, desc_adv(a, kstep_off(kk, C::HALF_BYTES)),
+                 desc_adv(bk, kstep_off(kk, C::HALF_BYTES)), idesc_qk, kk > 0);
       };
-      auto issue_pv = [&](int t, int slot, bool acc) {
-        const uint32_t b0 = sbase + C::OFF_V + slot * C::TILE_BYTES;
+      // O_t += P_t V_j over keys [64*half, 64*half + 64) of the tile
+      auto issue_pv_half = [&](int t, int slot, int half, bool acc) {
+        const uint64_t bv = slot ? dv1 : dv0;
+        const uint32_t d = tmem + C::tm_o(t);
+        const uint32_t a = tmem + C::tm_s(t);
 #pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {
-          mma_ts(tmem + C::tm_o(t), tmem + C::tm_s(t) + kk * 8,
-                 make_sdesc_sw128(b0 + kk * 16 * 128, C::HALF_BYTES, 1024), idesc_pv,
-                 (acc || kk > 0) ? 1u : 0u);
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = 4 * half + k4;
+          mma_ts(d, a + kk * 8, desc_adv(bv, kk * 16 * 128), idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(bar(FB_QFULL), 0, abort_flag, 201);
@@ -213,25 +224,43 @@ __global__ void __launch_bounds__(320, 1)
       if (ok && n_iter > 0) {
         tc_fence_after();
         for (int t = 0; t < 2; ++t)
-          if (nkv[t] > 0) {
+          if (nkv(t) > 0) {
             issue_qk(t, 0);
             tc_commit(bar(FB_SFULL + t));
           }
         tc_commit(bar(FB_KEMPTY + 0));
       }
+      // Slot-release commits of the previous iteration, issued once the next
+      // batch of MMAs is queued (a commit covers every MMA issued before it).
+      int pend_v = -1, pend_k = -1;
       for (int j = 0; j < n_iter && ok; ++j) {
         const int s = j & 1;
         const int sn = (j + 1) & 1;
-        ok = mbar_wait(bar(FB_VFULL + s), (j >> 1) & 1, abort_flag, 203);
-        if (!ok) break;
-        bool k_next_ready = false;
+        bool v_ready = false, k_next_ready = false;
         for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= nkv[t]) continue;
-          ok = mbar_wait(bar(FB_PFULL + t), j & 1, abort_flag, 204);
+          if (j >= nkv(t)) continue;
+          if (!v_ready) {
+            ok = mbar_wait(bar(FB_VFULL + s), (j >> 1) & 1, abort_flag, 203);
+            if (!ok) break;
+            v_ready = true;
+          }
+          ok = mbar_wait(bar(FB_PFULL + t), j & 1, abort_flag, 204);  // keys 0..63 of P_t(j)
           if (!ok) break;
           tc_fence_after();
-          issue_pv(t, s, j > 0);
-          if (j + 1 < nkv[t]) {
+          issue_pv_half(t, s, 0, j > 0);
+          if (pend_v >= 0) {
+            tc_commit(bar(FB_VEMPTY + pend_v));
+            pend_v = -1;
+          }
+          if (pend_k >= 0) {
+            tc_commit(bar(FB_KEMPTY + pend_k));
+            pend_k = -1;
+          }
+          ok = mbar_wait(bar(FB_PFULL1 + t), j & 1, abort_flag, 207);  // keys 64..127
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv_half(t, s, 1, true);
+          if (j + 1 < nkv(t)) {
             if (!k_next_ready) {
               ok = mbar_wait(bar(FB_KFULL + sn), ((j + 1) >> 1) & 1, abort_flag, 205);
               if (!ok) break;
@@ -245,8 +274,8 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         if (!ok) break;
-        tc_commit(bar(FB_VEMPTY + s));
-        if (j + 1 < n_iter) tc_commit(bar(FB_KEMPTY + sn));
+        pend_v = s;
+        pend_k = (j + 1 < n_iter) ? sn : -1;
       }
       // Drain: every MMA issued above completes before TMEM is released.
       tc_commit(bar(FB_DRAIN));
@@ -265,7 +294,7 @@ __global__ void __launch_bounds__(320, 1)
     const float sl2 = p.scale_log2;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < nkv[t]; ++j) {
+    for (int j = 0; j < nkv(t); ++j) {
       ok = mbar_wait(bar(FB_SFULL + t), j & 1, abort_flag, 300 + t);
       ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
       if (!ok) break;
@@ -285,49 +314,67 @@ __global__ void __launch_bounds__(320, 1)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      float rmax = -INFINITY;
+      // row max: 3-input max, four independent chains
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) rmax = fmaxf(rmax, __uint_as_float(sr[c][i]));
+        for (int i = 0; i < 32; i += 2)
+          mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], __uint_as_float(sr[c][i]),
+                                   __uint_as_float(sr[c][i + 1]));
+      const float rmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       const float m_new = fmaxf(m, rmax * sl2);
       const bool resc = m_new > m + 8.0f;
       const float m_use = resc ? m_new : m;
       const float alpha = resc ? ex2_approx(m - m_use) : 1.0f;
       const float base = (m_use == -INFINITY) ? 0.0f : m_use;
-      float rsum = 0.0f;
-      uint32_t pk[2][32];
+      const uint64_t sl2x2 = f2_make(sl2, sl2);
+      const uint64_t nbx2 = f2_make(-base, -base);
+      uint64_t acc2[2] = {f2_make(0.0f, 0.0f), f2_make(0.0f, 0.0f)};
+      // P = 2^(s*scale*log2e - m) in bf16, written over the S columns already
+      // read, 32 keys per store; handed off per 64-key half.
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int half = 0; half < 2; ++half) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), sl2, -base));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), sl2, -base));
-          rsum += p0 + p1;
-          pk[c >> 1][(c & 1) * 16 + i] = pack_bf16x2(p0, p1);
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint64_t x2 = f2_fma(
+                f2_make(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])), sl2x2,
+                nbx2);
+            float x0, x1;
+            f2_split(x2, x0, x1);
+            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+            acc2[i & 1] = f2_add(acc2[i & 1], f2_make(p0, p1));
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(tS + c * 16, pk);
         }
-      l = l * alpha + rsum;
-      tmem_st32(tS + 0, pk[0]);
-      tmem_st32(tS + 32, pk[1]);
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-        // PV(j-1) of this tile completed before S(j) was signalled.
+        if (half == 0 && j > 0 && __any_sync(0xffffffffu, resc)) {
+          // PV(j-1) of this tile completed before S(j) was signalled.
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t orow[32];
-          tmem_ld32(tO + c * 32, orow);
-          tmem_wait_ld();
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t orow[32];
+            tmem_ld32(tO + c * 32, orow);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-          tmem_st32(tO + c * 32, orow);
+            for (int i = 0; i < 32; ++i)
+              orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+            tmem_st32(tO + c * 32, orow);
+          }
         }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar((half == 0 ? FB_PFULL : FB_PFULL1) + t));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(FB_PFULL + t));
+      float a0, a1, a2, a3;
+      f2_split(acc2[0], a0, a1);
+      f2_split(acc2[1], a2, a3);
+      l = l * alpha + ((a0 + a1) + (a2 + a3));
       m = m_use;
     }
-    if (ok && nkv[t] > 0) {
+    if (ok && nkv(t) > 0) {
       ok = mbar_wait(bar(FB_ODONE + t), 0, abort_flag, 310 + t);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {

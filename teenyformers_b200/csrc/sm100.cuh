@@ -69,7 +69,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Waits for the phase with the given parity to complete.  Returns false (and
 // raises the CTA abort flag / device status) if it did not complete within
-// kWaitTimeoutNs, or if another role of the CTA already aborted.
+// kWaitTimeoutNs, or if another role of the CTA already aborted.  A null
+// abort_flag waits without looking at other roles (used to drain in-flight
+// async copies before the CTA exits).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           volatile int* abort_flag, int site) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -78,9 +80,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
+    if (abort_flag != nullptr && *abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-      *abort_flag = 1;
+      if (abort_flag != nullptr) *abort_flag = 1;
       atomicCAS(&g_device_status, 0, site);
       return false;
     }
@@ -210,6 +212,19 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
   return d;
 }
 
+// Advances a descriptor's start address by `bytes` (a multiple of 16).  The
+// start-address field is the low 14 bits (address >> 4) and shared memory is
+// below 256 KB, so the add never carries into the other fields.
+__device__ __forceinline__ uint64_t desc_adv(uint64_t desc, uint32_t bytes) {
+  return desc + (bytes >> 4);
+}
+
+// Byte offset of the 16-element K step kk inside a K-major SW128 tile stored
+// as 64-column halves of HALF_BYTES each.
+__host__ __device__ constexpr uint32_t kstep_off(int kk, int half_bytes) {
+  return uint32_t((kk >> 2) * half_bytes + (kk & 3) * 32);
+}
+
 // D[tmem] (+)= A[smem desc] * B[smem desc]
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate) {
@@ -245,6 +260,39 @@ __device__ __forceinline__ float lg2_approx(float x) {
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed fp32 pairs (Blackwell f32x2 FMA/ADD: one instruction, two lanes of
+// work).  A pair is held as one 64-bit register (lo = first element).
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Packs (lo, hi) into one bf16x2 word, round-to-nearest-even.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;

@@ -12,9 +12,14 @@ F32_ABS = 1e-4
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
+    """||a - b|| / ||b||.  When the reference is (numerically) zero -- e.g. dQ
+    of a single-key row, where dS = P (dP - D) = 0 exactly -- the ratio is
+    meaningless; the denominator is floored at 1e-3 RMS so the max-abs bound
+    decides."""
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
-    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+    floor = 1e-3 * np.sqrt(max(b.size, 1))
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), floor))
 
 
 def assert_bf16_close(name, got, ref, max_abs=BF16_MAX_ABS, rl2=BF16_REL_L2):

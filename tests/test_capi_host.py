@@ -73,7 +73,6 @@ def test_bwd_workspace_size(native_lib):
 
 def test_bwd_rejects_bad_arguments(native_lib):
     args = [FAKE] * 10 + [1, 4, 2, 64, 64, 128, 0.1, 1, None]
-    assert _capi.raw("tf_b200_flash_attn2_bwd_bf16", *args) != TF_OK or True
     bad = list(args)
     bad[9] = None  # workspace
     assert _capi.raw("tf_b200_flash_attn2_bwd_bf16", *bad) == TF_ERR_INVALID_ARG
