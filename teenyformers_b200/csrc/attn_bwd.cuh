@@ -232,33 +232,41 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 5) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0 && n_tiles > 0) {
+    // ---------------- TMA producer (whole warp, one elected lane issues) --------
+    if (n_tiles > 0) {
       int issued0 = 0, issued1 = 0;
       bool ok = true;
-      mbar_arrive_expect_tx(bar(KB_KV), 2 * C::TILE_BYTES);
-      for (int hh = 0; hh < C::HALVES; ++hh) {
-        tma_load_3d(sbase + C::OFF_K + hh * C::HALF_BYTES, &tm_k, bar(KB_KV), hh * 64, k0, bh_kv);
-        tma_load_3d(sbase + C::OFF_V + hh * C::HALF_BYTES, &tm_v, bar(KB_KV), hh * 64, k0, bh_kv);
+      if (elect_one()) {
+        mbar_arrive_expect_tx(bar(KB_KV), 2 * C::TILE_BYTES);
+        for (int hh = 0; hh < C::HALVES; ++hh) {
+          tma_load_3d(sbase + C::OFF_K + hh * C::HALF_BYTES, &tm_k, bar(KB_KV), hh * 64, k0,
+                      bh_kv);
+          tma_load_3d(sbase + C::OFF_V + hh * C::HALF_BYTES, &tm_v, bar(KB_KV), hh * 64, k0,
+                      bh_kv);
+        }
       }
+      __syncwarp();
       for (int it = 0; it < n_tiles && ok; ++it) {
         const int st = it & 1, u = it >> 1;
-        if (u > 0) ok = mbar_wait(bar(KB_QEMPTY + st), (u - 1) & 1, abort_flag, 401);
+        if (u > 0) ok = mbar_wait_warp(bar(KB_QEMPTY + st), (u - 1) & 1, abort_flag, 401);
         if (!ok) break;
         const int g = it / qt_per_head;
         const int qi = qt_first + it % qt_per_head;
         const int bh_q = b * p.Hq + hk * G + g;
         const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
-        mbar_arrive_expect_tx(bar(KB_QFULL + st), 2 * C::TILE_BYTES + 1024);
-        for (int hh = 0; hh < C::HALVES; ++hh) {
-          tma_load_3d(sb + C::STAGE_Q + hh * C::HALF_BYTES, &tm_q, bar(KB_QFULL + st), hh * 64,
-                      qi * 128, bh_q);
-          tma_load_3d(sb + C::STAGE_DO + hh * C::HALF_BYTES, &tm_do, bar(KB_QFULL + st),
-                      hh * 64, qi * 128, bh_q);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(bar(KB_QFULL + st), 2 * C::TILE_BYTES + 1024);
+          for (int hh = 0; hh < C::HALVES; ++hh) {
+            tma_load_3d(sb + C::STAGE_Q + hh * C::HALF_BYTES, &tm_q, bar(KB_QFULL + st),
+                        hh * 64, qi * 128, bh_q);
+            tma_load_3d(sb + C::STAGE_DO + hh * C::HALF_BYTES, &tm_do, bar(KB_QFULL + st),
+                        hh * 64, qi * 128, bh_q);
+          }
+          const size_t ws_off = (size_t)bh_q * p.Sq_pad + (size_t)qi * 128;
+          bulk_load(sb + C::STAGE_LSE, p.ws_lse2 + ws_off, 512, bar(KB_QFULL + st));
+          bulk_load(sb + C::STAGE_DELTA, p.ws_delta + ws_off, 512, bar(KB_QFULL + st));
         }
-        const size_t ws_off = (size_t)bh_q * p.Sq_pad + (size_t)qi * 128;
-        bulk_load(sb + C::STAGE_LSE, p.ws_lse2 + ws_off, 512, bar(KB_QFULL + st));
-        bulk_load(sb + C::STAGE_DELTA, p.ws_delta + ws_off, 512, bar(KB_QFULL + st));
+        __syncwarp();
         (st ? issued1 : issued0) += 1;
       }
       if (!ok) {
@@ -268,8 +276,8 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 4) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0 && n_tiles > 0) {
+    // ---------------- MMA issuer (whole warp, one elected lane issues) ----------
+    if (n_tiles > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
       constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);
       const uint64_t d_k = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_K);
@@ -278,69 +286,70 @@ __global__ void __launch_bounds__(192, 1)
       const uint64_t d_do0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::STAGE_DO);
       const uint64_t m_q0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::STAGE_Q);
       const uint64_t m_do0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::STAGE_DO);
-      // S^T_h = K Q_h^T and dP^T_h = V dO_h^T for stage st
+      // S^T_h = K Q_h^T and dP^T_h = V dO_h^T for stage st, then signal s_full[h]
       auto issue_s = [&](int h, int st) {
-        const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
-        const uint64_t bq = desc_adv(d_q0, so), bdo = desc_adv(d_do0, so);
-        const uint32_t dst = tmem + C::tm_st(h), ddp = tmem + C::tm_dpt(h);
+        if (elect_one()) {
+          const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
+          const uint64_t bq = desc_adv(d_q0, so), bdo = desc_adv(d_do0, so);
+          const uint32_t dst = tmem + C::tm_st(h), ddp = tmem + C::tm_dpt(h);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(dst, desc_adv(d_k, kstep_off(kk, C::HALF_BYTES)),
-                 desc_adv(bq, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss(dst, desc_adv(d_k, kstep_off(kk, C::HALF_BYTES)),
+                   desc_adv(bq, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(ddp, desc_adv(d_v, kstep_off(kk, C::HALF_BYTES)),
-                 desc_adv(bdo, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss(ddp, desc_adv(d_v, kstep_off(kk, C::HALF_BYTES)),
+                   desc_adv(bdo, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+          tc_commit(bar(KB_SFULL + h));
+        }
+        __syncwarp();
       };
-      // dV += P^T_h dO_h, dK += dS^T_h Q_h
-      auto issue_acc = [&](int h, int st, bool acc) {
-        const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
-        const uint64_t bdo = desc_adv(m_do0, so), bq = desc_adv(m_q0, so);
-        const uint32_t ap = tmem + C::tm_st(h), ads = tmem + C::tm_dpt(h);
+      // dV += P^T_h dO_h, dK += dS^T_h Q_h; then an optional commit
+      auto issue_acc = [&](int h, int st, bool acc, int commit) {
+        if (elect_one()) {
+          const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
+          const uint64_t bdo = desc_adv(m_do0, so), bq = desc_adv(m_q0, so);
+          const uint32_t ap = tmem + C::tm_st(h), ads = tmem + C::tm_dpt(h);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ts(tmem + C::TM_DV, ap + kk * 8, desc_adv(bdo, kk * 16 * 128), idesc_acc,
-                 (acc || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tmem + C::TM_DV, ap + kk * 8, desc_adv(bdo, kk * 16 * 128), idesc_acc,
+                   (acc || kk > 0) ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ts(tmem + C::TM_DK, ads + kk * 8, desc_adv(bq, kk * 16 * 128), idesc_acc,
-                 (acc || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tmem + C::TM_DK, ads + kk * 8, desc_adv(bq, kk * 16 * 128), idesc_acc,
+                   (acc || kk > 0) ? 1u : 0u);
+          if (commit >= 0) tc_commit(bar(commit));
+        }
+        __syncwarp();
       };
-      bool ok = mbar_wait(bar(KB_KV), 0, abort_flag, 411);
-      if (ok) ok = mbar_wait(bar(KB_QFULL + 0), 0, abort_flag, 412);
+      bool ok = mbar_wait_warp(bar(KB_KV), 0, abort_flag, 411);
+      if (ok) ok = mbar_wait_warp(bar(KB_QFULL + 0), 0, abort_flag, 412);
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
-        tc_commit(bar(KB_SFULL + 0));
         issue_s(1, 0);
-        tc_commit(bar(KB_SFULL + 1));
       }
       for (int it = 0; it < n_tiles && ok; ++it) {
         const int st = it & 1;
         const bool more = it + 1 < n_tiles;
-        ok = mbar_wait(bar(KB_PFULL + 0), it & 1, abort_flag, 413);
+        ok = mbar_wait_warp(bar(KB_PFULL + 0), it & 1, abort_flag, 413);
         if (!ok) break;
         tc_fence_after();
-        issue_acc(0, st, it > 0);
+        issue_acc(0, st, it > 0, -1);
         if (more) {
-          ok = mbar_wait(bar(KB_QFULL + (st ^ 1)), ((it + 1) >> 1) & 1, abort_flag, 414);
+          ok = mbar_wait_warp(bar(KB_QFULL + (st ^ 1)), ((it + 1) >> 1) & 1, abort_flag, 414);
           if (!ok) break;
           tc_fence_after();
           issue_s(0, st ^ 1);
-          tc_commit(bar(KB_SFULL + 0));
         }
-        ok = mbar_wait(bar(KB_PFULL + 1), it & 1, abort_flag, 415);
+        ok = mbar_wait_warp(bar(KB_PFULL + 1), it & 1, abort_flag, 415);
         if (!ok) break;
         tc_fence_after();
-        issue_acc(1, st, true);
-        tc_commit(bar(KB_QEMPTY + st));
-        if (more) {
-          issue_s(1, st ^ 1);
-          tc_commit(bar(KB_SFULL + 1));
-        }
+        issue_acc(1, st, true, more ? KB_QEMPTY + st : KB_ACC);
+        if (more) issue_s(1, st ^ 1);
       }
-      if (ok) tc_commit(bar(KB_ACC));
-      tc_commit(bar(KB_DRAIN));
+      if (elect_one()) tc_commit(bar(KB_DRAIN));
+      __syncwarp();
       mbar_wait_noabort(bar(KB_DRAIN), 0, 416);
     }
   } else {
@@ -485,19 +494,23 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 5) {
-    if (lane == 0) {
-      int issued0 = 0, issued1 = 0;
-      bool ok = true;
+    // ---------------- TMA producer (whole warp, one elected lane issues) --------
+    int issued0 = 0, issued1 = 0;
+    bool ok = true;
+    if (elect_one()) {
       mbar_arrive_expect_tx(bar(QB_Q), 2 * C::TILE_BYTES);
       for (int hh = 0; hh < C::HALVES; ++hh) {
         tma_load_3d(sbase + C::OFF_Q + hh * C::HALF_BYTES, &tm_q, bar(QB_Q), hh * 64, q0, bh);
         tma_load_3d(sbase + C::OFF_DO + hh * C::HALF_BYTES, &tm_do, bar(QB_Q), hh * 64, q0, bh);
       }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j & 1, u = j >> 1;
-        if (u > 0) ok = mbar_wait(bar(QB_KVEMPTY + st), (u - 1) & 1, abort_flag, 501);
-        if (!ok) break;
-        const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
+    }
+    __syncwarp();
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const int st = j & 1, u = j >> 1;
+      if (u > 0) ok = mbar_wait_warp(bar(QB_KVEMPTY + st), (u - 1) & 1, abort_flag, 501);
+      if (!ok) break;
+      const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
+      if (elect_one()) {
         mbar_arrive_expect_tx(bar(QB_KVFULL + st), 2 * C::TILE_BYTES);
         for (int hh = 0; hh < C::HALVES; ++hh) {
           tma_load_3d(sb + hh * C::HALF_BYTES, &tm_k, bar(QB_KVFULL + st), hh * 64, j * 128,
@@ -505,25 +518,27 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_3d(sb + C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v, bar(QB_KVFULL + st),
                       hh * 64, j * 128, bh_kv);
         }
-        (st ? issued1 : issued0) += 1;
       }
-      if (!ok) {
-        mbar_wait_noabort(bar(QB_Q), 0, 502);
-        if (issued0) mbar_wait_noabort(bar(QB_KVFULL + 0), (issued0 - 1) & 1, 502);
-        if (issued1) mbar_wait_noabort(bar(QB_KVFULL + 1), (issued1 - 1) & 1, 502);
-      }
+      __syncwarp();
+      (st ? issued1 : issued0) += 1;
+    }
+    if (!ok) {
+      mbar_wait_noabort(bar(QB_Q), 0, 502);
+      if (issued0) mbar_wait_noabort(bar(QB_KVFULL + 0), (issued0 - 1) & 1, 502);
+      if (issued1) mbar_wait_noabort(bar(QB_KVFULL + 1), (issued1 - 1) & 1, 502);
     }
   } else if (warp == 4) {
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
-      constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
-      const uint64_t d_q = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_Q);
-      const uint64_t d_do = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_DO);
-      const uint64_t d_k0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
-      const uint64_t d_v0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::TILE_BYTES);
-      const uint64_t m_k0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
-      // S_h = Q K_h^T, dP_h = dO V_h^T for key stage st
-      auto issue_s = [&](int h, int st) {
+    // ---------------- MMA issuer (whole warp, one elected lane issues) ----------
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
+    constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
+    const uint64_t d_q = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_Q);
+    const uint64_t d_do = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_DO);
+    const uint64_t d_k0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
+    const uint64_t d_v0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::TILE_BYTES);
+    const uint64_t m_k0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
+    // S_h = Q K_h^T, dP_h = dO V_h^T for key stage st, then signal s_full[h]
+    auto issue_s = [&](int h, int st) {
+      if (elect_one()) {
         const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
         const uint64_t bk = desc_adv(d_k0, so), bv = desc_adv(d_v0, so);
         const uint32_t ds = tmem + C::tm_s(h), ddp = tmem + C::tm_dp(h);
@@ -535,53 +550,52 @@ __global__ void __launch_bounds__(192, 1)
         for (int kk = 0; kk < D / 16; ++kk)
           mma_ss(ddp, desc_adv(d_do, kstep_off(kk, C::HALF_BYTES)),
                  desc_adv(bv, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
-      };
-      // dQ += dS_h K_h
-      auto issue_dq = [&](int h, int st, bool acc) {
+        tc_commit(bar(QB_SFULL + h));
+      }
+      __syncwarp();
+    };
+    // dQ += dS_h K_h; then an optional commit
+    auto issue_dq = [&](int h, int st, bool acc, int commit) {
+      if (elect_one()) {
         const uint64_t bk = desc_adv(m_k0, st * C::STAGE_BYTES + h * 64 * 128);
         const uint32_t a = tmem + C::tm_s(h);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_ts(tmem + C::TM_DQ, a + kk * 8, desc_adv(bk, kk * 16 * 128), idesc_dq,
                  (acc || kk > 0) ? 1u : 0u);
-      };
-      bool ok = mbar_wait(bar(QB_Q), 0, abort_flag, 511);
-      if (ok) ok = mbar_wait(bar(QB_KVFULL + 0), 0, abort_flag, 512);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        tc_commit(bar(QB_SFULL + 0));
-        issue_s(1, 0);
-        tc_commit(bar(QB_SFULL + 1));
+        if (commit >= 0) tc_commit(bar(commit));
       }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j & 1;
-        const bool more = j + 1 < n_kv;
-        ok = mbar_wait(bar(QB_PFULL + 0), j & 1, abort_flag, 513);
-        if (!ok) break;
-        tc_fence_after();
-        issue_dq(0, st, j > 0);
-        if (more) {
-          ok = mbar_wait(bar(QB_KVFULL + (st ^ 1)), ((j + 1) >> 1) & 1, abort_flag, 514);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(0, st ^ 1);
-          tc_commit(bar(QB_SFULL + 0));
-        }
-        ok = mbar_wait(bar(QB_PFULL + 1), j & 1, abort_flag, 515);
-        if (!ok) break;
-        tc_fence_after();
-        issue_dq(1, st, true);
-        tc_commit(bar(QB_KVEMPTY + st));
-        if (more) {
-          issue_s(1, st ^ 1);
-          tc_commit(bar(QB_SFULL + 1));
-        }
-      }
-      if (ok) tc_commit(bar(QB_ACC));
-      tc_commit(bar(QB_DRAIN));
-      mbar_wait_noabort(bar(QB_DRAIN), 0, 516);
+      __syncwarp();
+    };
+    bool ok = mbar_wait_warp(bar(QB_Q), 0, abort_flag, 511);
+    if (ok) ok = mbar_wait_warp(bar(QB_KVFULL + 0), 0, abort_flag, 512);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
     }
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const int st = j & 1;
+      const bool more = j + 1 < n_kv;
+      ok = mbar_wait_warp(bar(QB_PFULL + 0), j & 1, abort_flag, 513);
+      if (!ok) break;
+      tc_fence_after();
+      issue_dq(0, st, j > 0, -1);
+      if (more) {
+        ok = mbar_wait_warp(bar(QB_KVFULL + (st ^ 1)), ((j + 1) >> 1) & 1, abort_flag, 514);
+        if (!ok) break;
+        tc_fence_after();
+        issue_s(0, st ^ 1);
+      }
+      ok = mbar_wait_warp(bar(QB_PFULL + 1), j & 1, abort_flag, 515);
+      if (!ok) break;
+      tc_fence_after();
+      issue_dq(1, st, true, more ? QB_KVEMPTY + st : QB_ACC);
+      if (more) issue_s(1, st ^ 1);
+    }
+    if (elect_one()) tc_commit(bar(QB_DRAIN));
+    __syncwarp();
+    mbar_wait_noabort(bar(QB_DRAIN), 0, 516);
   } else {
     const int row = warp * 32 + lane;
     const uint32_t lane_base = uint32_t(warp * 32) << 16;

@@ -151,55 +151,63 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 9) {
-    // =================== TMA producer ===================
-    if (lane == 0) {
-      int issued_k0 = 0, issued_k1 = 0, issued_v0 = 0, issued_v1 = 0;
-      bool ok = true;
+    // =================== TMA producer (whole warp, one elected lane issues) =====
+    int issued_k0 = 0, issued_k1 = 0, issued_v0 = 0, issued_v1 = 0;
+    bool ok = true;
+    if (elect_one()) {
       mbar_arrive_expect_tx(bar(FB_QFULL), 2 * C::TILE_BYTES);
       for (int t = 0; t < 2; ++t)
         for (int hh = 0; hh < C::HALVES; ++hh)
           tma_load_3d(sbase + C::OFF_Q + t * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_q,
                       bar(FB_QFULL), hh * 64, q0 + 128 * t, bh);
-      for (int j = 0; j < n_iter && ok; ++j) {
-        const int s = j & 1, u = j >> 1;
-        if (u > 0) ok = mbar_wait(bar(FB_KEMPTY + s), (u - 1) & 1, abort_flag, 101);
-        if (!ok) break;
+    }
+    __syncwarp();
+    for (int j = 0; j < n_iter && ok; ++j) {
+      const int s = j & 1, u = j >> 1;
+      if (u > 0) ok = mbar_wait_warp(bar(FB_KEMPTY + s), (u - 1) & 1, abort_flag, 101);
+      if (!ok) break;
+      if (elect_one()) {
         mbar_arrive_expect_tx(bar(FB_KFULL + s), C::TILE_BYTES);
         for (int hh = 0; hh < C::HALVES; ++hh)
           tma_load_3d(sbase + C::OFF_K + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_k,
                       bar(FB_KFULL + s), hh * 64, j * 128, bh_kv);
-        (s ? issued_k1 : issued_k0) += 1;
-        if (u > 0) ok = mbar_wait(bar(FB_VEMPTY + s), (u - 1) & 1, abort_flag, 102);
-        if (!ok) break;
+      }
+      __syncwarp();
+      (s ? issued_k1 : issued_k0) += 1;
+      if (u > 0) ok = mbar_wait_warp(bar(FB_VEMPTY + s), (u - 1) & 1, abort_flag, 102);
+      if (!ok) break;
+      if (elect_one()) {
         mbar_arrive_expect_tx(bar(FB_VFULL + s), C::TILE_BYTES);
         for (int hh = 0; hh < C::HALVES; ++hh)
           tma_load_3d(sbase + C::OFF_V + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v,
                       bar(FB_VFULL + s), hh * 64, j * 128, bh_kv);
-        (s ? issued_v1 : issued_v0) += 1;
       }
-      if (!ok) {
-        // Abort: let every issued copy land before the CTA's smem goes away.
-        mbar_drain_wait(bar(FB_QFULL), 0, 103);
-        if (issued_k0) mbar_drain_wait(bar(FB_KFULL + 0), (issued_k0 - 1) & 1, 103);
-        if (issued_k1) mbar_drain_wait(bar(FB_KFULL + 1), (issued_k1 - 1) & 1, 103);
-        if (issued_v0) mbar_drain_wait(bar(FB_VFULL + 0), (issued_v0 - 1) & 1, 103);
-        if (issued_v1) mbar_drain_wait(bar(FB_VFULL + 1), (issued_v1 - 1) & 1, 103);
-      }
+      __syncwarp();
+      (s ? issued_v1 : issued_v0) += 1;
+    }
+    if (!ok) {
+      // Abort: let every issued copy land before the CTA's smem goes away.
+      mbar_drain_wait(bar(FB_QFULL), 0, 103);
+      if (issued_k0) mbar_drain_wait(bar(FB_KFULL + 0), (issued_k0 - 1) & 1, 103);
+      if (issued_k1) mbar_drain_wait(bar(FB_KFULL + 1), (issued_k1 - 1) & 1, 103);
+      if (issued_v0) mbar_drain_wait(bar(FB_VFULL + 0), (issued_v0 - 1) & 1, 103);
+      if (issued_v1) mbar_drain_wait(bar(FB_VFULL + 1), (issued_v1 - 1) & 1, 103);
     }
   } else if (warp == 8) {
-    // =================== MMA issuer ===================
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = make_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t idesc_pv = make_idesc_bf16(128, D, 0, 1);
-      // Descriptors are built once; each K step only advances the start
-      // address by a compile-time constant.
-      const uint64_t dq0 = make_sdesc_sw128(sbase + C::OFF_Q, 16, 1024);
-      const uint64_t dq1 = desc_adv(dq0, C::TILE_BYTES);
-      const uint64_t dk0 = make_sdesc_sw128(sbase + C::OFF_K, 16, 1024);
-      const uint64_t dk1 = desc_adv(dk0, C::TILE_BYTES);
-      const uint64_t dv0 = make_sdesc_sw128(sbase + C::OFF_V, C::HALF_BYTES, 1024);
-      const uint64_t dv1 = desc_adv(dv0, C::TILE_BYTES);
-      auto issue_qk = [&](int t, int slot) {
+    // =================== MMA issuer (whole warp, one elected lane issues) =======
+    constexpr uint32_t idesc_qk = make_idesc_bf16(128, 128, 0, 0);
+    constexpr uint32_t idesc_pv = make_idesc_bf16(128, D, 0, 1);
+    // Descriptors are built once; each K step only advances the start
+    // address by a compile-time constant.
+    const uint64_t dq0 = make_sdesc_sw128(sbase + C::OFF_Q, 16, 1024);
+    const uint64_t dq1 = desc_adv(dq0, C::TILE_BYTES);
+    const uint64_t dk0 = make_sdesc_sw128(sbase + C::OFF_K, 16, 1024);
+    const uint64_t dk1 = desc_adv(dk0, C::TILE_BYTES);
+    const uint64_t dv0 = make_sdesc_sw128(sbase + C::OFF_V, C::HALF_BYTES, 1024);
+    const uint64_t dv1 = desc_adv(dv0, C::TILE_BYTES);
+    // S_t = Q_t K_slot^T, then signal s_full[t]
+    auto issue_qk = [&](int t, int slot) {
+      if (elect_one()) {
         const uint64_t a = t ? dq1 : dq0;
         const uint64_t bk = slot ? dk1 : dk0;
         const uint32_t d = tmem + C::tm_s(t);
@@ -207,80 +215,80 @@ __global__ void __launch_bounds__(320, 1)
         for (int kk = 0; kk < D / 16; ++kk)
           mma_ss(d, desc_adv(a, kstep_off(kk, C::HALF_BYTES)),
                  desc_adv(bk, kstep_off(kk, C::HALF_BYTES)), idesc_qk, kk > 0);
-      };
-      // O_t += P_t V_j over keys [64*half, 64*half + 64) of the tile
-      auto issue_pv_half = [&](int t, int slot, int half, bool acc) {
+        tc_commit(bar(FB_SFULL + t));
+      }
+      __syncwarp();
+    };
+    // O_t += P_t V_j over keys [64*half, 64*half + 64) of the tile; then the
+    // optional commits (a commit covers every MMA issued before it).
+    auto issue_pv_half = [&](int t, int slot, int half, bool acc, int commit0, int commit1) {
+      if (elect_one()) {
         const uint64_t bv = slot ? dv1 : dv0;
         const uint32_t d = tmem + C::tm_o(t);
         const uint32_t a = tmem + C::tm_s(t);
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
           const int kk = 4 * half + k4;
-          mma_ts(d, a + kk * 8, desc_adv(bv, kk * 16 * 128), idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          mma_ts(d, a + kk * 8, desc_adv(bv, kk * 16 * 128), idesc_pv,
+                 (acc || kk > 0) ? 1u : 0u);
         }
-      };
-      bool ok = mbar_wait(bar(FB_QFULL), 0, abort_flag, 201);
-      if (ok && n_iter > 0) ok = mbar_wait(bar(FB_KFULL + 0), 0, abort_flag, 202);
-      if (ok && n_iter > 0) {
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t)
-          if (nkv(t) > 0) {
-            issue_qk(t, 0);
-            tc_commit(bar(FB_SFULL + t));
-          }
-        tc_commit(bar(FB_KEMPTY + 0));
+        if (commit0 >= 0) tc_commit(bar(commit0));
+        if (commit1 >= 0) tc_commit(bar(commit1));
       }
-      // Slot-release commits of the previous iteration, issued once the next
-      // batch of MMAs is queued (a commit covers every MMA issued before it).
-      int pend_v = -1, pend_k = -1;
-      for (int j = 0; j < n_iter && ok; ++j) {
-        const int s = j & 1;
-        const int sn = (j + 1) & 1;
-        bool v_ready = false, k_next_ready = false;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= nkv(t)) continue;
-          if (!v_ready) {
-            ok = mbar_wait(bar(FB_VFULL + s), (j >> 1) & 1, abort_flag, 203);
-            if (!ok) break;
-            v_ready = true;
-          }
-          ok = mbar_wait(bar(FB_PFULL + t), j & 1, abort_flag, 204);  // keys 0..63 of P_t(j)
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv_half(t, s, 0, j > 0);
-          if (pend_v >= 0) {
-            tc_commit(bar(FB_VEMPTY + pend_v));
-            pend_v = -1;
-          }
-          if (pend_k >= 0) {
-            tc_commit(bar(FB_KEMPTY + pend_k));
-            pend_k = -1;
-          }
-          ok = mbar_wait(bar(FB_PFULL1 + t), j & 1, abort_flag, 207);  // keys 64..127
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv_half(t, s, 1, true);
-          if (j + 1 < nkv(t)) {
-            if (!k_next_ready) {
-              ok = mbar_wait(bar(FB_KFULL + sn), ((j + 1) >> 1) & 1, abort_flag, 205);
-              if (!ok) break;
-              tc_fence_after();
-              k_next_ready = true;
-            }
-            issue_qk(t, sn);
-            tc_commit(bar(FB_SFULL + t));
-          } else {
-            tc_commit(bar(FB_ODONE + t));
-          }
-        }
-        if (!ok) break;
-        pend_v = s;
-        pend_k = (j + 1 < n_iter) ? sn : -1;
-      }
-      // Drain: every MMA issued above completes before TMEM is released.
-      tc_commit(bar(FB_DRAIN));
-      mbar_drain_wait(bar(FB_DRAIN), 0, 206);
+      __syncwarp();
+    };
+    bool ok = mbar_wait_warp(bar(FB_QFULL), 0, abort_flag, 201);
+    if (ok && n_iter > 0) ok = mbar_wait_warp(bar(FB_KFULL + 0), 0, abort_flag, 202);
+    if (ok && n_iter > 0) {
+      tc_fence_after();
+      for (int t = 0; t < 2; ++t)
+        if (nkv(t) > 0) issue_qk(t, 0);
+      if (elect_one()) tc_commit(bar(FB_KEMPTY + 0));
+      __syncwarp();
     }
+    // Slot-release commits of the previous iteration are issued once the next
+    // batch of MMAs is queued.
+    int pend_v = -1, pend_k = -1;
+    for (int j = 0; j < n_iter && ok; ++j) {
+      const int s = j & 1;
+      const int sn = (j + 1) & 1;
+      bool v_ready = false, k_next_ready = false;
+      for (int t = 0; t < 2 && ok; ++t) {
+        if (j >= nkv(t)) continue;
+        if (!v_ready) {
+          ok = mbar_wait_warp(bar(FB_VFULL + s), (j >> 1) & 1, abort_flag, 203);
+          if (!ok) break;
+          v_ready = true;
+        }
+        ok = mbar_wait_warp(bar(FB_PFULL + t), j & 1, abort_flag, 204);  // keys 0..63 of P_t(j)
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv_half(t, s, 0, j > 0, pend_v >= 0 ? FB_VEMPTY + pend_v : -1,
+                      pend_k >= 0 ? FB_KEMPTY + pend_k : -1);
+        pend_v = pend_k = -1;
+        ok = mbar_wait_warp(bar(FB_PFULL1 + t), j & 1, abort_flag, 207);  // keys 64..127
+        if (!ok) break;
+        tc_fence_after();
+        const bool more = j + 1 < nkv(t);
+        issue_pv_half(t, s, 1, true, more ? -1 : FB_ODONE + t, -1);
+        if (more) {
+          if (!k_next_ready) {
+            ok = mbar_wait_warp(bar(FB_KFULL + sn), ((j + 1) >> 1) & 1, abort_flag, 205);
+            if (!ok) break;
+            tc_fence_after();
+            k_next_ready = true;
+          }
+          issue_qk(t, sn);
+        }
+      }
+      if (!ok) break;
+      pend_v = s;
+      pend_k = (j + 1 < n_iter) ? sn : -1;
+    }
+    // Drain: every MMA issued above completes before TMEM is released.
+    if (elect_one()) tc_commit(bar(FB_DRAIN));
+    __syncwarp();
+    mbar_drain_wait(bar(FB_DRAIN), 0, 206);
   } else {
     // =================== softmax: warps 0-3 tile 0, 4-7 tile 1 ===================
     const int t = warp >> 2;

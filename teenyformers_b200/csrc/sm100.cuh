@@ -89,6 +89,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// One lane of a converged warp (elect.sync).  Producer / MMA warps run their
+// loops with all 32 lanes so loop state stays warp-uniform, and only the
+// elected lane issues TMA copies, MMAs and commits.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// mbar_wait by every lane of a warp, with a warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, int site) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tiled, no multicast)
 // ---------------------------------------------------------------------------
