@@ -11,9 +11,10 @@
 // zero-initialisation.
 //
 // Three kernels, all single-CTA tcgen05 (no clusters, no multicast):
-//  1. fa_bwd_prep_kernel: D_q and LSE*log2(e) per query row into the
-//     workspace ([BHq, Sq_pad] each, padded rows get D=0, LSE=+inf so
-//     their P is exactly 0).
+//  1. fa_bwd_prep_kernel: -D_q and -LSE*log2(e) per query row into the
+//     workspace ([BHq, Sq_pad] each; stored negated so the elementwise
+//     passes are one packed FMA / ADD; padded rows get 0 and -inf so their
+//     P is exactly 0).
 //  2. fa_bwd_dkdv_sm100_kernel: one CTA per 128-key tile of one KV head,
 //     looping over the 128-row query tiles of every query head of the GQA
 //     group.  Each query tile is processed as two 64-query halves h so the
@@ -27,11 +28,18 @@
 //     MMAs of half 0 are queued (tcgen05 MMAs of one thread run in order).
 //  3. fa_bwd_dq_sm100_kernel: one CTA per 128-row query tile, looping over
 //     key tiles in two 64-key halves: S_h = Q K_h^T, dP_h = dO V_h^T,
-//     dS_h (bf16) over S_h, dQ += dS_h K_h.  TMEM: S_0 S_1 dP_0 dP_1 as
-//     above, dQ [256,256+D).
-// Roles: warps 0-3 elementwise (one TMEM lane = one row per thread),
-// warp 4 MMA issuer, warp 5 TMA producer.
+//     dS_h (bf16) over S_h, dQ += dS_h K_h.  Q and dO are copied into TMEM
+//     once, so S_h and dP_h are TS MMAs (A from TMEM; only K/V are read
+//     from shared memory, which keeps N=64 MMAs at full rate).  TMEM:
+//     S_0 S_1 dP_0 dP_1 as above, dQ [256,256+D), Q [384,384+D/2),
+//     dO [384+D/2, 384+D).  K/V stream through a 3-stage ring.
+// Roles (both kernels): warps 0-3 elementwise for half 0 and warps 4-7 for
+// half 1 (one TMEM lane = one row per thread, the two halves run
+// concurrently), warp 8 MMA issuer, warp 9 TMA producer; the issuer and
+// producer loops run on the whole warp and one elected lane issues.
 #pragma once
+
+#include <type_traits>
 
 #include "sm100.cuh"
 
@@ -74,8 +82,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (sub == 0) {
-    ws_delta[row] = acc;
-    ws_lse2[row] = qi < Sq ? lse[(size_t)bh * Sq + qi] * 1.4426950408889634f : INFINITY;
+    ws_delta[row] = -acc;
+    ws_lse2[row] = qi < Sq ? -lse[(size_t)bh * Sq + qi] * 1.4426950408889634f : -INFINITY;
   }
 }
 
@@ -84,8 +92,8 @@ struct BwdParams {
   __nv_bfloat16* dq;
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
-  const float* ws_lse2;
-  const float* ws_delta;
+  const float* ws_lse2;   // -LSE * log2(e)
+  const float* ws_delta;  // -rowsum(O * dO)
   int Sq, Sk, Sq_pad;
   int Hq, Hkv;
   int BHq, BHkv;
@@ -110,7 +118,7 @@ __device__ __forceinline__ void mbar_wait_noabort(uint32_t bar, uint32_t parity,
 
 template <int D>
 struct BwdKvCfg {
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;
   static constexpr int HALVES = D / 64;
   static constexpr int HALF_BYTES = 128 * 128;
   static constexpr int TILE_BYTES = 128 * D * 2;
@@ -132,17 +140,16 @@ struct BwdKvCfg {
 
 template <int D>
 struct BwdQCfg {
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;
   static constexpr int HALVES = D / 64;
   static constexpr int HALF_BYTES = 128 * 128;
   static constexpr int TILE_BYTES = 128 * D * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_DO = TILE_BYTES;
-  static constexpr int OFF_STAGE = 2 * TILE_BYTES;  // 2 stages of {K, V}
+  static constexpr int KV_STAGES = 3;
+  static constexpr int OFF_STAGE = 0;  // KV_STAGES stages of {K, V}
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_STAGE + 2 * STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_STAGE + KV_STAGES * STAGE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
-  static constexpr uint32_t TM_DQ = 256;
+  static constexpr uint32_t TM_DQ = 256, TM_Q = 384, TM_DO = 384 + D / 2;
   static constexpr uint32_t TM_COLS = 512;
   __device__ static constexpr uint32_t tm_s(int h) { return uint32_t(h) * 64u; }
   __device__ static constexpr uint32_t tm_dp(int h) { return 128u + uint32_t(h) * 64u; }
@@ -150,8 +157,8 @@ struct BwdQCfg {
 
 enum BwdKvBar { KB_KV = 0, KB_QFULL = 1, KB_QEMPTY = 3, KB_SFULL = 5, KB_PFULL = 7,
                 KB_ACC = 9, KB_DRAIN = 10, KB_COUNT = 11 };
-enum BwdQBar { QB_Q = 0, QB_KVFULL = 1, QB_KVEMPTY = 3, QB_SFULL = 5, QB_PFULL = 7,
-               QB_ACC = 9, QB_DRAIN = 10, QB_COUNT = 11 };
+enum BwdQBar { QB_Q = 0, QB_KVFULL = 1, QB_KVEMPTY = 4, QB_SFULL = 7, QB_PFULL = 9,
+               QB_ACC = 11, QB_DRAIN = 12, QB_COUNT = 13 };
 
 // Stores one 32-column fp32 TMEM chunk (scaled) as 32 bf16 to global.
 __device__ __forceinline__ void store_row_chunk_bf16(__nv_bfloat16* dst, const uint32_t (&r)[32],
@@ -183,7 +190,7 @@ __device__ __forceinline__ uint64_t mnmajor_base(uint32_t tile) {
 
 // ------------------------------------------------------------------ dK / dV
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_do,
                              const __grid_constant__ CUtensorMap tm_k,
@@ -199,9 +206,10 @@ __global__ void __launch_bounds__(192, 1)
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // Heavy first: key tile 0 has the most query tiles under the causal mask.
-  const int kt = blockIdx.x / p.BHkv;
-  const int bh_kv = blockIdx.x % p.BHkv;
+  // Head-major (a head's Q/dO stay hot in L2 while its key tiles run), and
+  // within a head key tile 0 first: it has the most query tiles when causal.
+  const int bh_kv = blockIdx.x / p.n_kt;
+  const int kt = blockIdx.x % p.n_kt;
   const int b = bh_kv / p.Hkv, hk = bh_kv % p.Hkv;
   const int G = p.Hq / p.Hkv;
   const int k0 = kt * 128;
@@ -231,7 +239,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ---------------- TMA producer (whole warp, one elected lane issues) --------
     if (n_tiles > 0) {
       int issued0 = 0, issued1 = 0;
@@ -275,7 +283,7 @@ __global__ void __launch_bounds__(192, 1)
         if (issued1) mbar_wait_noabort(bar(KB_QFULL + 1), (issued1 - 1) & 1, 402);
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ---------------- MMA issuer (whole warp, one elected lane issues) ----------
     if (n_tiles > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
@@ -353,9 +361,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait_noabort(bar(KB_DRAIN), 0, 416);
     }
   } else {
-    // ---------------- elementwise: warps 0-3, thread = key row ----------------
-    const int row = warp * 32 + lane;
-    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    // ------------- elementwise: warps 0-3 half 0, warps 4-7 half 1; thread = key row
+    const int h = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_base = uint32_t(wq * 32) << 16;
     const int key = k0 + row;
     const float sl2 = p.scale_log2;
     bool ok = true;
@@ -367,70 +377,74 @@ __global__ void __launch_bounds__(192, 1)
       const float4* s_delta = reinterpret_cast<const float4*>(sb + C::STAGE_DELTA);
       const bool diag = p.causal && qi * 128 < k0 + 127;
       const int qlim = key - qi * 128;  // query columns with index < qlim are hidden (k > q)
-#pragma unroll 1
-      for (int h = 0; h < 2 && ok; ++h) {
-        ok = mbar_wait(bar(KB_SFULL + h), it & 1, abort_flag, 421);
-        if (ok && h == 0) ok = mbar_wait(bar(KB_QFULL + st), (it >> 1) & 1, abort_flag, 422);
-        ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          const int col0 = h * 64 + c * 32;  // query column of this chunk within the tile
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tmem + lane_base + C::tm_st(h) + c * 32, sr);
-          tmem_ld32(tmem + lane_base + C::tm_dpt(h) + c * 32, dr);
-          tmem_wait_ld();
-          uint32_t pk[16], dk[16];
+      ok = mbar_wait(bar(KB_SFULL + h), it & 1, abort_flag, 421);
+      if (ok) ok = mbar_wait(bar(KB_QFULL + st), (it >> 1) & 1, abort_flag, 422);
+      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+      if (!ok) break;
+      tc_fence_after();
+      // P^T = 2^(s*scale*log2e - lse), dS^T = P^T * (dP^T - D), both packed
+      // to bf16 over the columns already read; 32 query columns per chunk.
+      auto chunk = [&](auto mask_tag, int c) {
+        constexpr bool kMask = decltype(mask_tag)::value;
+        const int col0 = h * 64 + c * 32;  // query column of this chunk within the tile
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_base + C::tm_st(h) + c * 32, sr);
+        tmem_ld32(tmem + lane_base + C::tm_dpt(h) + c * 32, dr);
+        tmem_wait_ld();
+        uint32_t pk[16], dk[16];
 #pragma unroll
-          for (int v4 = 0; v4 < 8; ++v4) {
-            const float4 l4 = s_lse[col0 / 4 + v4];
-            const float4 d4 = s_delta[col0 / 4 + v4];
-            const float lq[4] = {l4.x, l4.y, l4.z, l4.w};
-            const float dq[4] = {d4.x, d4.y, d4.z, d4.w};
-            float pv[4], dsv[4];
+        for (int v4 = 0; v4 < 8; ++v4) {
+          const float4 l4 = s_lse[col0 / 4 + v4];    // -lse2
+          const float4 d4 = s_delta[col0 / 4 + v4];  // -D
+          const float nl[4] = {l4.x, l4.y, l4.z, l4.w};
+          const float nd[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pv[4], dsv[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = v4 * 4 + e;
-              float pe = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, -lq[e]));
-              if (diag && col0 + i < qlim) pe = 0.0f;
-              pv[e] = pe;
-              dsv[e] = pe * (__uint_as_float(dr[i]) - dq[e]);
-            }
-            pk[2 * v4] = pack_bf16x2(pv[0], pv[1]);
-            pk[2 * v4 + 1] = pack_bf16x2(pv[2], pv[3]);
-            dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
-            dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
+          for (int e = 0; e < 4; ++e) {
+            const int i = v4 * 4 + e;
+            float pe = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, nl[e]));
+            if (kMask && col0 + i < qlim) pe = 0.0f;
+            pv[e] = pe;
+            dsv[e] = pe * (__uint_as_float(dr[i]) + nd[e]);
           }
-          tmem_st16(tmem + lane_base + C::tm_st(h) + c * 16, pk);
-          tmem_st16(tmem + lane_base + C::tm_dpt(h) + c * 16, dk);
+          pk[2 * v4] = pack_bf16x2(pv[0], pv[1]);
+          pk[2 * v4 + 1] = pack_bf16x2(pv[2], pv[3]);
+          dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
+          dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar(KB_PFULL + h));
+        tmem_st16(tmem + lane_base + C::tm_st(h) + c * 16, pk);
+        tmem_st16(tmem + lane_base + C::tm_dpt(h) + c * 16, dk);
+      };
+      if (diag) {
+        chunk(std::true_type{}, 0);
+        chunk(std::true_type{}, 1);
+      } else {
+        chunk(std::false_type{}, 0);
+        chunk(std::false_type{}, 1);
       }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(KB_PFULL + h));
     }
-    // ---- epilogue: dV = acc, dK = acc * scale ----
+    // ---- epilogue: warps 0-3 write dV = acc, warps 4-7 dK = acc * scale ----
     const bool valid = key < p.Sk;
-    __nv_bfloat16* dv_row = p.dv + ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D;
-    __nv_bfloat16* dk_row = p.dk + ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D;
+    __nv_bfloat16* out_row =
+        (h == 0 ? p.dv : p.dk) + ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D;
     if (n_tiles == 0) {
       if (valid) {
-        uint4* a = reinterpret_cast<uint4*>(dv_row);
-        uint4* bb = reinterpret_cast<uint4*>(dk_row);
-        for (int v4 = 0; v4 < D / 8; ++v4) a[v4] = bb[v4] = make_uint4(0, 0, 0, 0);
+        uint4* a4 = reinterpret_cast<uint4*>(out_row);
+        for (int v4 = 0; v4 < D / 8; ++v4) a4[v4] = make_uint4(0, 0, 0, 0);
       }
     } else if (__all_sync(0xffffffffu, ok && mbar_wait(bar(KB_ACC), 0, abort_flag, 423))) {
       tc_fence_after();
+      const uint32_t acc_col = h == 0 ? C::TM_DV : C::TM_DK;
+      const float mul = h == 0 ? 1.0f : p.scale;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + C::TM_DV + c * 32, r);
+        tmem_ld32(tmem + lane_base + acc_col + c * 32, r);
         tmem_wait_ld();
-        if (valid) store_row_chunk_bf16(dv_row + c * 32, r, 1.0f);
-        tmem_ld32(tmem + lane_base + C::TM_DK + c * 32, r);
-        tmem_wait_ld();
-        if (valid) store_row_chunk_bf16(dk_row + c * 32, r, p.scale);
+        if (valid) store_row_chunk_bf16(out_row + c * 32, r, mul);
       }
     }
   }
@@ -445,11 +459,11 @@ __global__ void __launch_bounds__(192, 1)
 
 // ------------------------------------------------------------------ dQ
 template <int D>
-__global__ void __launch_bounds__(192, 1)
-    fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
-                           const __grid_constant__ CUtensorMap tm_do,
-                           const __grid_constant__ CUtensorMap tm_k,
-                           const __grid_constant__ CUtensorMap tm_v, const BwdParams p) {
+__global__ void __launch_bounds__(320, 1)
+    fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v, const BwdParams p,
+                           const __nv_bfloat16* __restrict__ q,
+                           const __nv_bfloat16* __restrict__ dO) {
   using C = BwdQCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -472,10 +486,12 @@ __global__ void __launch_bounds__(192, 1)
   if (p.causal) n_kv = min(p.n_kt, (min(p.Sq, q0 + 128) - 1) / 128 + 1);
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(QB_Q), 1);
-    for (int s = 0; s < 2; ++s) {
+    mbar_init(bar(QB_Q), 256);
+    for (int s = 0; s < C::KV_STAGES; ++s) {
       mbar_init(bar(QB_KVFULL + s), 1);
       mbar_init(bar(QB_KVEMPTY + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar(QB_SFULL + s), 1);
       mbar_init(bar(QB_PFULL + s), 128);
     }
@@ -493,20 +509,12 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ---------------- TMA producer (whole warp, one elected lane issues) --------
-    int issued0 = 0, issued1 = 0;
+    int issued[C::KV_STAGES] = {};
     bool ok = true;
-    if (elect_one()) {
-      mbar_arrive_expect_tx(bar(QB_Q), 2 * C::TILE_BYTES);
-      for (int hh = 0; hh < C::HALVES; ++hh) {
-        tma_load_3d(sbase + C::OFF_Q + hh * C::HALF_BYTES, &tm_q, bar(QB_Q), hh * 64, q0, bh);
-        tma_load_3d(sbase + C::OFF_DO + hh * C::HALF_BYTES, &tm_do, bar(QB_Q), hh * 64, q0, bh);
-      }
-    }
-    __syncwarp();
     for (int j = 0; j < n_kv && ok; ++j) {
-      const int st = j & 1, u = j >> 1;
+      const int st = j % C::KV_STAGES, u = j / C::KV_STAGES;
       if (u > 0) ok = mbar_wait_warp(bar(QB_KVEMPTY + st), (u - 1) & 1, abort_flag, 501);
       if (!ok) break;
       const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
@@ -520,23 +528,23 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       __syncwarp();
-      (st ? issued1 : issued0) += 1;
+#pragma unroll
+      for (int s2 = 0; s2 < C::KV_STAGES; ++s2) issued[s2] += (s2 == st);
     }
     if (!ok) {
-      mbar_wait_noabort(bar(QB_Q), 0, 502);
-      if (issued0) mbar_wait_noabort(bar(QB_KVFULL + 0), (issued0 - 1) & 1, 502);
-      if (issued1) mbar_wait_noabort(bar(QB_KVFULL + 1), (issued1 - 1) & 1, 502);
+#pragma unroll
+      for (int s2 = 0; s2 < C::KV_STAGES; ++s2)
+        if (issued[s2]) mbar_wait_noabort(bar(QB_KVFULL + s2), (issued[s2] - 1) & 1, 502);
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ---------------- MMA issuer (whole warp, one elected lane issues) ----------
     constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
     constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
-    const uint64_t d_q = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_Q);
-    const uint64_t d_do = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_DO);
     const uint64_t d_k0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
     const uint64_t d_v0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::TILE_BYTES);
     const uint64_t m_k0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
-    // S_h = Q K_h^T, dP_h = dO V_h^T for key stage st, then signal s_full[h]
+    // S_h = Q K_h^T, dP_h = dO V_h^T for key stage st (A = Q / dO in TMEM),
+    // then signal s_full[h]
     auto issue_s = [&](int h, int st) {
       if (elect_one()) {
         const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
@@ -544,12 +552,12 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ds = tmem + C::tm_s(h), ddp = tmem + C::tm_dp(h);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(ds, desc_adv(d_q, kstep_off(kk, C::HALF_BYTES)),
-                 desc_adv(bk, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+          mma_ts(ds, tmem + C::TM_Q + kk * 8, desc_adv(bk, kstep_off(kk, C::HALF_BYTES)), idesc_s,
+                 kk > 0);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(ddp, desc_adv(d_do, kstep_off(kk, C::HALF_BYTES)),
-                 desc_adv(bv, kstep_off(kk, C::HALF_BYTES)), idesc_s, kk > 0);
+          mma_ts(ddp, tmem + C::TM_DO + kk * 8, desc_adv(bv, kstep_off(kk, C::HALF_BYTES)),
+                 idesc_s, kk > 0);
         tc_commit(bar(QB_SFULL + h));
       }
       __syncwarp();
@@ -575,34 +583,60 @@ __global__ void __launch_bounds__(192, 1)
       issue_s(1, 0);
     }
     for (int j = 0; j < n_kv && ok; ++j) {
-      const int st = j & 1;
+      const int st = j % C::KV_STAGES;
+      const int stn = (j + 1) % C::KV_STAGES;
       const bool more = j + 1 < n_kv;
       ok = mbar_wait_warp(bar(QB_PFULL + 0), j & 1, abort_flag, 513);
       if (!ok) break;
       tc_fence_after();
       issue_dq(0, st, j > 0, -1);
       if (more) {
-        ok = mbar_wait_warp(bar(QB_KVFULL + (st ^ 1)), ((j + 1) >> 1) & 1, abort_flag, 514);
+        ok = mbar_wait_warp(bar(QB_KVFULL + stn), ((j + 1) / C::KV_STAGES) & 1, abort_flag, 514);
         if (!ok) break;
         tc_fence_after();
-        issue_s(0, st ^ 1);
+        issue_s(0, stn);
       }
       ok = mbar_wait_warp(bar(QB_PFULL + 1), j & 1, abort_flag, 515);
       if (!ok) break;
       tc_fence_after();
       issue_dq(1, st, true, more ? QB_KVEMPTY + st : QB_ACC);
-      if (more) issue_s(1, st ^ 1);
+      if (more) issue_s(1, stn);
     }
     if (elect_one()) tc_commit(bar(QB_DRAIN));
     __syncwarp();
     mbar_wait_noabort(bar(QB_DRAIN), 0, 516);
   } else {
-    const int row = warp * 32 + lane;
-    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    // ------------- elementwise: warps 0-3 keys 0-63, warps 4-7 keys 64-127 of
+    // each tile; thread = query row
+    const int h = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_base = uint32_t(wq * 32) << 16;
     const int qrow = q0 + row;
+    // Q (warps 0-3) / dO (warps 4-7) row into TMEM as the MMAs' A operand.
+    {
+      const __nv_bfloat16* src = (h == 0 ? q : dO) + ((size_t)bh * p.Sq + qrow) * D;
+      const bool in = qrow < p.Sq;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t w[16];
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const uint4 x = in ? reinterpret_cast<const uint4*>(src)[c * 4 + v4] : make_uint4(0, 0, 0, 0);
+          w[4 * v4] = x.x;
+          w[4 * v4 + 1] = x.y;
+          w[4 * v4 + 2] = x.z;
+          w[4 * v4 + 3] = x.w;
+        }
+        tmem_st16(tmem + lane_base + (h == 0 ? C::TM_Q : C::TM_DO) + c * 16, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(QB_Q));
+    }
     const size_t ws_idx = (size_t)bh * p.Sq_pad + qrow;  // qrow < Sq_pad always
-    const float lse2 = p.ws_lse2[ws_idx];
-    const float delta = p.ws_delta[ws_idx];
+    const float nlse2 = p.ws_lse2[ws_idx];   // -LSE * log2(e)
+    const float ndelta = p.ws_delta[ws_idx];  // -D
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
@@ -610,46 +644,52 @@ __global__ void __launch_bounds__(192, 1)
       const bool need_mask = (p.causal && kb + 127 > q0) || (kb + 128 > p.Sk);
       int lim = p.Sk - 1 - kb;  // key columns with index > lim are hidden
       if (p.causal) lim = min(lim, qrow - kb);
-#pragma unroll 1
-      for (int h = 0; h < 2 && ok; ++h) {
-        ok = mbar_wait(bar(QB_SFULL + h), j & 1, abort_flag, 521);
-        ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          const int col0 = h * 64 + c * 32;
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tmem + lane_base + C::tm_s(h) + c * 32, sr);
-          tmem_ld32(tmem + lane_base + C::tm_dp(h) + c * 32, dr);
-          tmem_wait_ld();
-          uint32_t dsk[16];
+      ok = mbar_wait(bar(QB_SFULL + h), j & 1, abort_flag, 521);
+      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+      if (!ok) break;
+      tc_fence_after();
+      // dS = 2^(s*scale*log2e - lse) * (dP - D), packed to bf16 over S.
+      auto chunk = [&](auto mask_tag, int c) {
+        constexpr bool kMask = decltype(mask_tag)::value;
+        const int col0 = h * 64 + c * 32;
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_base + C::tm_s(h) + c * 32, sr);
+        tmem_ld32(tmem + lane_base + C::tm_dp(h) + c * 32, dr);
+        tmem_wait_ld();
+        uint32_t dsk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -lse2));
-            float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -lse2));
-            if (need_mask) {
-              if (col0 + 2 * i > lim) p0 = 0.0f;
-              if (col0 + 2 * i + 1 > lim) p1 = 0.0f;
-            }
-            dsk[i] = pack_bf16x2(p0 * (__uint_as_float(dr[2 * i]) - delta),
-                                 p1 * (__uint_as_float(dr[2 * i + 1]) - delta));
+        for (int i = 0; i < 32; i += 2) {
+          float p0 = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, nlse2));
+          float p1 = ex2_approx(fmaf(__uint_as_float(sr[i + 1]), sl2, nlse2));
+          if (kMask) {
+            if (col0 + i > lim) p0 = 0.0f;
+            if (col0 + i + 1 > lim) p1 = 0.0f;
           }
-          tmem_st16(tmem + lane_base + C::tm_s(h) + c * 16, dsk);
+          dsk[i / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[i]) + ndelta),
+                                   p1 * (__uint_as_float(dr[i + 1]) + ndelta));
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar(QB_PFULL + h));
+        tmem_st16(tmem + lane_base + C::tm_s(h) + c * 16, dsk);
+      };
+      if (need_mask) {
+        chunk(std::true_type{}, 0);
+        chunk(std::true_type{}, 1);
+      } else {
+        chunk(std::false_type{}, 0);
+        chunk(std::false_type{}, 1);
       }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(QB_PFULL + h));
     }
+    // ---- epilogue: dQ = acc * scale; warps 0-3 columns [0, D/2), 4-7 [D/2, D)
     if (__all_sync(0xffffffffu, ok && mbar_wait(bar(QB_ACC), 0, abort_flag, 522))) {
       tc_fence_after();
       const bool valid = qrow < p.Sq;
-      __nv_bfloat16* dq_row = p.dq + ((size_t)bh * p.Sq + (valid ? qrow : 0)) * D;
+      __nv_bfloat16* dq_row = p.dq + ((size_t)bh * p.Sq + (valid ? qrow : 0)) * D + h * (D / 2);
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < D / 64; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + C::TM_DQ + c * 32, r);
+        tmem_ld32(tmem + lane_base + C::TM_DQ + h * (D / 2) + c * 32, r);
         tmem_wait_ld();
         if (valid) store_row_chunk_bf16(dq_row + c * 32, r, p.scale);
       }

@@ -258,12 +258,12 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const 
     fa_bwd_dkdv_sm100_kernel<128><<<grid_kv, BwdKvCfg<128>::kThreads, BwdKvCfg<128>::SMEM_BYTES,
                                     st>>>(tq, tdo, tk, tv, prm);
     fa_bwd_dq_sm100_kernel<128><<<grid_q, BwdQCfg<128>::kThreads, BwdQCfg<128>::SMEM_BYTES, st>>>(
-        tq, tdo, tk, tv, prm);
+        tk, tv, prm, static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(d_o));
   } else {
     fa_bwd_dkdv_sm100_kernel<64><<<grid_kv, BwdKvCfg<64>::kThreads, BwdKvCfg<64>::SMEM_BYTES,
                                    st>>>(tq, tdo, tk, tv, prm);
     fa_bwd_dq_sm100_kernel<64><<<grid_q, BwdQCfg<64>::kThreads, BwdQCfg<64>::SMEM_BYTES, st>>>(
-        tq, tdo, tk, tv, prm);
+        tk, tv, prm, static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(d_o));
   }
   return launch_status();
 }
