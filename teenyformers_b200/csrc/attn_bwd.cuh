@@ -33,10 +33,11 @@
 //     from shared memory, which keeps N=64 MMAs at full rate).  TMEM:
 //     S_0 S_1 dP_0 dP_1 as above, dQ [256,256+D), Q [384,384+D/2),
 //     dO [384+D/2, 384+D).  K/V stream through a 3-stage ring.
-// Roles (both kernels): warps 0-3 elementwise for half 0 and warps 4-7 for
-// half 1 (one TMEM lane = one row per thread, the two halves run
-// concurrently), warp 8 MMA issuer, warp 9 TMA producer; the issuer and
-// producer loops run on the whole warp and one elected lane issues.
+// Roles (both kernels): warps 0-15 elementwise, four warpgroups, one per
+// 32-column chunk c of half h (warpgroup 2h + c; one TMEM lane = one row per
+// thread), so each SM sub-partition runs four elementwise warps; warp 16
+// MMA issuer, warp 17 TMA producer.  The issuer and producer loops run on
+// the whole warp and one elected lane issues.
 #pragma once
 
 #include <type_traits>
@@ -116,9 +117,12 @@ __device__ __forceinline__ void mbar_wait_noabort(uint32_t bar, uint32_t parity,
   (void)mbar_wait(bar, parity, nullptr, site);
 }
 
+constexpr int kBwdThreads = 576;  // 16 elementwise warps + MMA warp + TMA warp
+constexpr int kBwdMmaWarp = 16, kBwdTmaWarp = 17;
+
 template <int D>
 struct BwdKvCfg {
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = kBwdThreads;
   static constexpr int HALVES = D / 64;
   static constexpr int HALF_BYTES = 128 * 128;
   static constexpr int TILE_BYTES = 128 * D * 2;
@@ -140,7 +144,7 @@ struct BwdKvCfg {
 
 template <int D>
 struct BwdQCfg {
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = kBwdThreads;
   static constexpr int HALVES = D / 64;
   static constexpr int HALF_BYTES = 128 * 128;
   static constexpr int TILE_BYTES = 128 * D * 2;
@@ -159,6 +163,13 @@ enum BwdKvBar { KB_KV = 0, KB_QFULL = 1, KB_QEMPTY = 3, KB_SFULL = 5, KB_PFULL =
                 KB_ACC = 9, KB_DRAIN = 10, KB_COUNT = 11 };
 enum BwdQBar { QB_Q = 0, QB_KVFULL = 1, QB_KVEMPTY = 4, QB_SFULL = 7, QB_PFULL = 9,
                QB_ACC = 11, QB_DRAIN = 12, QB_COUNT = 13 };
+
+// TMEM column (relative to a half's base) of the bf16-packed operand for
+// the 16-row K step kk of that half: the 64 rows are written as two 32-row
+// chunks, each packed into the first 16 columns of its own 32-column slot.
+__device__ __forceinline__ constexpr uint32_t packed_col(int kk) {
+  return uint32_t((kk >> 1) * 32 + (kk & 1) * 8);
+}
 
 // Stores one 32-column fp32 TMEM chunk (scaled) as 32 bf16 to global.
 __device__ __forceinline__ void store_row_chunk_bf16(__nv_bfloat16* dst, const uint32_t (&r)[32],
@@ -190,7 +201,7 @@ __device__ __forceinline__ uint64_t mnmajor_base(uint32_t tile) {
 
 // ------------------------------------------------------------------ dK / dV
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_do,
                              const __grid_constant__ CUtensorMap tm_k,
@@ -223,7 +234,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(KB_QFULL + s), 1);
       mbar_init(bar(KB_QEMPTY + s), 1);
       mbar_init(bar(KB_SFULL + s), 1);
-      mbar_init(bar(KB_PFULL + s), 128);
+      mbar_init(bar(KB_PFULL + s), 256);
     }
     mbar_init(bar(KB_ACC), 1);
     mbar_init(bar(KB_DRAIN), 1);
@@ -239,7 +250,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == kBwdTmaWarp) {
     // ---------------- TMA producer (whole warp, one elected lane issues) --------
     if (n_tiles > 0) {
       int issued0 = 0, issued1 = 0;
@@ -283,7 +294,7 @@ __global__ void __launch_bounds__(320, 1)
         if (issued1) mbar_wait_noabort(bar(KB_QFULL + 1), (issued1 - 1) & 1, 402);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == kBwdMmaWarp) {
     // ---------------- MMA issuer (whole warp, one elected lane issues) ----------
     if (n_tiles > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
@@ -320,11 +331,11 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t ap = tmem + C::tm_st(h), ads = tmem + C::tm_dpt(h);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + C::TM_DV, ap + kk * 8, desc_adv(bdo, kk * 16 * 128), idesc_acc,
+            mma_ts(tmem + C::TM_DV, ap + packed_col(kk), desc_adv(bdo, kk * 16 * 128), idesc_acc,
                    (acc || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + C::TM_DK, ads + kk * 8, desc_adv(bq, kk * 16 * 128), idesc_acc,
+            mma_ts(tmem + C::TM_DK, ads + packed_col(kk), desc_adv(bq, kk * 16 * 128), idesc_acc,
                    (acc || kk > 0) ? 1u : 0u);
           if (commit >= 0) tc_commit(bar(commit));
         }
@@ -361,13 +372,16 @@ __global__ void __launch_bounds__(320, 1)
       mbar_wait_noabort(bar(KB_DRAIN), 0, 416);
     }
   } else {
-    // ------------- elementwise: warps 0-3 half 0, warps 4-7 half 1; thread = key row
-    const int h = warp >> 2;
+    // ------------- elementwise: warpgroup 2h + c owns query columns
+    // [64h + 32c, 64h + 32c + 32) of every tile; thread = key row
+    const int wg = warp >> 2;
+    const int h = wg >> 1, cq = wg & 1;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_base = uint32_t(wq * 32) << 16;
     const int key = k0 + row;
     const float sl2 = p.scale_log2;
+    const int col0 = h * 64 + cq * 32;  // first query column of this warpgroup's chunk
     bool ok = true;
     for (int it = 0; it < n_tiles && ok; ++it) {
       const int st = it & 1;
@@ -382,20 +396,20 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
       if (!ok) break;
       tc_fence_after();
-      // P^T = 2^(s*scale*log2e - lse), dS^T = P^T * (dP^T - D), both packed
-      // to bf16 over the columns already read; 32 query columns per chunk.
-      auto chunk = [&](auto mask_tag, int c) {
+      // P^T = 2^(s*scale*log2e - lse), dS^T = P^T * (dP^T - D), both packed to
+      // bf16 over the columns already read; 16 query columns per step.
+      auto step = [&](auto mask_tag, int sub) {
         constexpr bool kMask = decltype(mask_tag)::value;
-        const int col0 = h * 64 + c * 32;  // query column of this chunk within the tile
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + C::tm_st(h) + c * 32, sr);
-        tmem_ld32(tmem + lane_base + C::tm_dpt(h) + c * 32, dr);
+        const int c0 = col0 + sub * 16;
+        uint32_t sr[16], dr[16];
+        tmem_ld16(tmem + lane_base + C::tm_st(h) + cq * 32 + sub * 16, sr);
+        tmem_ld16(tmem + lane_base + C::tm_dpt(h) + cq * 32 + sub * 16, dr);
         tmem_wait_ld();
-        uint32_t pk[16], dk[16];
+        uint32_t pk[8], dk[8];
 #pragma unroll
-        for (int v4 = 0; v4 < 8; ++v4) {
-          const float4 l4 = s_lse[col0 / 4 + v4];    // -lse2
-          const float4 d4 = s_delta[col0 / 4 + v4];  // -D
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const float4 l4 = s_lse[c0 / 4 + v4];    // -lse2
+          const float4 d4 = s_delta[c0 / 4 + v4];  // -D
           const float nl[4] = {l4.x, l4.y, l4.z, l4.w};
           const float nd[4] = {d4.x, d4.y, d4.z, d4.w};
           float pv[4], dsv[4];
@@ -403,7 +417,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int e = 0; e < 4; ++e) {
             const int i = v4 * 4 + e;
             float pe = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, nl[e]));
-            if (kMask && col0 + i < qlim) pe = 0.0f;
+            if (kMask && c0 + i < qlim) pe = 0.0f;
             pv[e] = pe;
             dsv[e] = pe * (__uint_as_float(dr[i]) + nd[e]);
           }
@@ -412,35 +426,38 @@ __global__ void __launch_bounds__(320, 1)
           dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
           dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
         }
-        tmem_st16(tmem + lane_base + C::tm_st(h) + c * 16, pk);
-        tmem_st16(tmem + lane_base + C::tm_dpt(h) + c * 16, dk);
+        // Packed output stays inside this warpgroup's own 32 read columns
+        // (the other warpgroup of the half may still be reading its own):
+        // chunk cq, step sub -> columns 32*cq + 8*sub of the half.
+        tmem_st8(tmem + lane_base + C::tm_st(h) + cq * 32 + sub * 8, pk);
+        tmem_st8(tmem + lane_base + C::tm_dpt(h) + cq * 32 + sub * 8, dk);
       };
       if (diag) {
-        chunk(std::true_type{}, 0);
-        chunk(std::true_type{}, 1);
+        step(std::true_type{}, 0);
+        step(std::true_type{}, 1);
       } else {
-        chunk(std::false_type{}, 0);
-        chunk(std::false_type{}, 1);
+        step(std::false_type{}, 0);
+        step(std::false_type{}, 1);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(KB_PFULL + h));
     }
-    // ---- epilogue: warps 0-3 write dV = acc, warps 4-7 dK = acc * scale ----
+    // ---- epilogue: warpgroups 0,1 write dV, 2,3 dK (= acc * scale), 64 columns each
     const bool valid = key < p.Sk;
-    __nv_bfloat16* out_row =
-        (h == 0 ? p.dv : p.dk) + ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D;
+    __nv_bfloat16* out_row = (h == 0 ? p.dv : p.dk) +
+                             ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D + cq * (D / 2);
     if (n_tiles == 0) {
       if (valid) {
         uint4* a4 = reinterpret_cast<uint4*>(out_row);
-        for (int v4 = 0; v4 < D / 8; ++v4) a4[v4] = make_uint4(0, 0, 0, 0);
+        for (int v4 = 0; v4 < D / 16; ++v4) a4[v4] = make_uint4(0, 0, 0, 0);
       }
     } else if (__all_sync(0xffffffffu, ok && mbar_wait(bar(KB_ACC), 0, abort_flag, 423))) {
       tc_fence_after();
-      const uint32_t acc_col = h == 0 ? C::TM_DV : C::TM_DK;
+      const uint32_t acc_col = (h == 0 ? C::TM_DV : C::TM_DK) + cq * (D / 2);
       const float mul = h == 0 ? 1.0f : p.scale;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < D / 64; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + acc_col + c * 32, r);
         tmem_wait_ld();
@@ -459,7 +476,7 @@ __global__ void __launch_bounds__(320, 1)
 
 // ------------------------------------------------------------------ dQ
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const BwdParams p,
                            const __nv_bfloat16* __restrict__ q,
@@ -486,14 +503,14 @@ __global__ void __launch_bounds__(320, 1)
   if (p.causal) n_kv = min(p.n_kt, (min(p.Sq, q0 + 128) - 1) / 128 + 1);
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(QB_Q), 256);
+    mbar_init(bar(QB_Q), 512);
     for (int s = 0; s < C::KV_STAGES; ++s) {
       mbar_init(bar(QB_KVFULL + s), 1);
       mbar_init(bar(QB_KVEMPTY + s), 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(QB_SFULL + s), 1);
-      mbar_init(bar(QB_PFULL + s), 128);
+      mbar_init(bar(QB_PFULL + s), 256);
     }
     mbar_init(bar(QB_ACC), 1);
     mbar_init(bar(QB_DRAIN), 1);
@@ -509,7 +526,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == kBwdTmaWarp) {
     // ---------------- TMA producer (whole warp, one elected lane issues) --------
     int issued[C::KV_STAGES] = {};
     bool ok = true;
@@ -536,7 +553,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int s2 = 0; s2 < C::KV_STAGES; ++s2)
         if (issued[s2]) mbar_wait_noabort(bar(QB_KVFULL + s2), (issued[s2] - 1) & 1, 502);
     }
-  } else if (warp == 8) {
+  } else if (warp == kBwdMmaWarp) {
     // ---------------- MMA issuer (whole warp, one elected lane issues) ----------
     constexpr uint32_t idesc_s = make_idesc_bf16(128, 64, 0, 0);
     constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
@@ -569,7 +586,7 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t a = tmem + C::tm_s(h);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_ts(tmem + C::TM_DQ, a + kk * 8, desc_adv(bk, kk * 16 * 128), idesc_dq,
+          mma_ts(tmem + C::TM_DQ, a + packed_col(kk), desc_adv(bk, kk * 16 * 128), idesc_dq,
                  (acc || kk > 0) ? 1u : 0u);
         if (commit >= 0) tc_commit(bar(commit));
       }
@@ -606,29 +623,31 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
     mbar_wait_noabort(bar(QB_DRAIN), 0, 516);
   } else {
-    // ------------- elementwise: warps 0-3 keys 0-63, warps 4-7 keys 64-127 of
-    // each tile; thread = query row
-    const int h = warp >> 2;
+    // ------------- elementwise: warpgroup 2h + c owns key columns
+    // [64h + 32c, 64h + 32c + 32) of every tile; thread = query row
+    const int wg = warp >> 2;
+    const int h = wg >> 1, cq = wg & 1;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_base = uint32_t(wq * 32) << 16;
     const int qrow = q0 + row;
-    // Q (warps 0-3) / dO (warps 4-7) row into TMEM as the MMAs' A operand.
+    // Q (warpgroups 0,1) / dO (2,3) row halves into TMEM as the MMAs' A operand.
     {
-      const __nv_bfloat16* src = (h == 0 ? q : dO) + ((size_t)bh * p.Sq + qrow) * D;
+      const __nv_bfloat16* src = (h == 0 ? q : dO) + ((size_t)bh * p.Sq + qrow) * D + cq * (D / 2);
       const bool in = qrow < p.Sq;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < D / 64; ++c) {
         uint32_t w[16];
 #pragma unroll
         for (int v4 = 0; v4 < 4; ++v4) {
-          const uint4 x = in ? reinterpret_cast<const uint4*>(src)[c * 4 + v4] : make_uint4(0, 0, 0, 0);
+          const uint4 x =
+              in ? reinterpret_cast<const uint4*>(src)[c * 4 + v4] : make_uint4(0, 0, 0, 0);
           w[4 * v4] = x.x;
           w[4 * v4 + 1] = x.y;
           w[4 * v4 + 2] = x.z;
           w[4 * v4 + 3] = x.w;
         }
-        tmem_st16(tmem + lane_base + (h == 0 ? C::TM_Q : C::TM_DO) + c * 16, w);
+        tmem_st16(tmem + lane_base + (h == 0 ? C::TM_Q : C::TM_DO) + cq * (D / 4) + c * 16, w);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -638,6 +657,7 @@ __global__ void __launch_bounds__(320, 1)
     const float nlse2 = p.ws_lse2[ws_idx];   // -LSE * log2(e)
     const float ndelta = p.ws_delta[ws_idx];  // -D
     const float sl2 = p.scale_log2;
+    const int col0 = h * 64 + cq * 32;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
       const int kb = j * 128;
@@ -648,50 +668,66 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
       if (!ok) break;
       tc_fence_after();
-      // dS = 2^(s*scale*log2e - lse) * (dP - D), packed to bf16 over S.
-      auto chunk = [&](auto mask_tag, int c) {
+      // dS = 2^(s*scale*log2e - lse) * (dP - D), packed to bf16 inside this
+      // warpgroup's own columns (see packed_col), 16 keys per step.
+      auto step = [&](auto mask_tag, int sub) {
         constexpr bool kMask = decltype(mask_tag)::value;
-        const int col0 = h * 64 + c * 32;
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + C::tm_s(h) + c * 32, sr);
-        tmem_ld32(tmem + lane_base + C::tm_dp(h) + c * 32, dr);
+        const int c0 = col0 + sub * 16;
+        uint32_t sr[16], dr[16];
+        tmem_ld16(tmem + lane_base + C::tm_s(h) + cq * 32 + sub * 16, sr);
+        tmem_ld16(tmem + lane_base + C::tm_dp(h) + cq * 32 + sub * 16, dr);
         tmem_wait_ld();
-        uint32_t dsk[16];
+        uint32_t dsk[8];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
+        for (int i = 0; i < 16; i += 2) {
           float p0 = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, nlse2));
           float p1 = ex2_approx(fmaf(__uint_as_float(sr[i + 1]), sl2, nlse2));
           if (kMask) {
-            if (col0 + i > lim) p0 = 0.0f;
-            if (col0 + i + 1 > lim) p1 = 0.0f;
+            if (c0 + i > lim) p0 = 0.0f;
+            if (c0 + i + 1 > lim) p1 = 0.0f;
           }
           dsk[i / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[i]) + ndelta),
                                    p1 * (__uint_as_float(dr[i + 1]) + ndelta));
         }
-        tmem_st16(tmem + lane_base + C::tm_s(h) + c * 16, dsk);
+        tmem_st8(tmem + lane_base + C::tm_s(h) + cq * 32 + sub * 8, dsk);
       };
       if (need_mask) {
-        chunk(std::true_type{}, 0);
-        chunk(std::true_type{}, 1);
+        step(std::true_type{}, 0);
+        step(std::true_type{}, 1);
       } else {
-        chunk(std::false_type{}, 0);
-        chunk(std::false_type{}, 1);
+        step(std::false_type{}, 0);
+        step(std::false_type{}, 1);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(QB_PFULL + h));
     }
-    // ---- epilogue: dQ = acc * scale; warps 0-3 columns [0, D/2), 4-7 [D/2, D)
+    // ---- epilogue: dQ = acc * scale; warpgroup wg writes columns [wg*D/4, (wg+1)*D/4)
     if (__all_sync(0xffffffffu, ok && mbar_wait(bar(QB_ACC), 0, abort_flag, 522))) {
       tc_fence_after();
       const bool valid = qrow < p.Sq;
-      __nv_bfloat16* dq_row = p.dq + ((size_t)bh * p.Sq + (valid ? qrow : 0)) * D + h * (D / 2);
+      __nv_bfloat16* dq_row = p.dq + ((size_t)bh * p.Sq + (valid ? qrow : 0)) * D + wg * (D / 4);
 #pragma unroll 1
-      for (int c = 0; c < D / 64; ++c) {
+      for (int c = 0; c < D / 128; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + C::TM_DQ + h * (D / 2) + c * 32, r);
+        tmem_ld32(tmem + lane_base + C::TM_DQ + wg * (D / 4) + c * 32, r);
         tmem_wait_ld();
         if (valid) store_row_chunk_bf16(dq_row + c * 32, r, p.scale);
+      }
+      if (D / 4 == 16) {  // D = 64: 16 columns per warpgroup
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + C::TM_DQ + wg * (D / 4), r);
+        tmem_wait_ld();
+        if (valid) {
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            w[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * p.scale,
+                               __uint_as_float(r[2 * i + 1]) * p.scale);
+          uint4* d4 = reinterpret_cast<uint4*>(dq_row);
+          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       }
     }
   }
