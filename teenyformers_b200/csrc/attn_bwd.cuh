@@ -162,7 +162,7 @@ struct BwdQCfg {
 enum BwdKvBar { KB_KV = 0, KB_QFULL = 1, KB_QEMPTY = 3, KB_SFULL = 5, KB_PFULL = 7,
                 KB_ACC = 9, KB_DRAIN = 10, KB_COUNT = 11 };
 enum BwdQBar { QB_Q = 0, QB_KVFULL = 1, QB_KVEMPTY = 4, QB_SFULL = 7, QB_PFULL = 9,
-               QB_ACC = 11, QB_DRAIN = 12, QB_COUNT = 13 };
+               QB_ACC = 11, QB_DRAIN = 12, QB_QFREE = 13, QB_DQFREE = 14, QB_COUNT = 15 };
 
 // TMEM column (relative to a half's base) of the bf16-packed operand for
 // the 16-row K step kk of that half: the 64 rows are written as two 32-row
@@ -475,6 +475,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 // ------------------------------------------------------------------ dQ
+// Persistent: gridDim.x CTAs (one per SM) walk the work items in rounds of
+// gridDim.x, boustrophedon order (sched_item), so every CTA gets a mix of
+// heavy and light items; item w is query tile qi of head bh, head-major
+// (a few heads' K/V hot in L2 at a time) with heavy (late) query tiles first
+// under the causal mask.  The K/V ring, the per-half S / P barriers and TMEM carry over from
+// item to item; the next item's Q / dO rows are prefetched into registers
+// while the current item runs, staged into TMEM as soon as its last S MMA
+// has drained (QB_QFREE), and the MMA warp starts the next item's S MMAs
+// while the elementwise warps run the current item's epilogue.
+struct DqItem {
+  int bh, qi, q0, n_kv, bh_kv;
+};
+
+// Item of round k for this CTA: rounds alternate direction so the heavy
+// items at the start of each head spread evenly over the CTAs.  Only the
+// last round can be partial, so an out-of-range item means "no more".
+__device__ __forceinline__ int sched_item(int k) {
+  const int G = gridDim.x, c = blockIdx.x;
+  return k * G + ((k & 1) ? G - 1 - c : c);
+}
+
+__device__ __forceinline__ DqItem dq_item(const BwdParams& p, int w) {
+  DqItem it;
+  it.bh = w / p.n_qt;
+  it.qi = w % p.n_qt;
+  if (p.causal) it.qi = p.n_qt - 1 - it.qi;
+  it.q0 = it.qi * 128;
+  it.n_kv = p.n_kt;
+  if (p.causal) it.n_kv = min(p.n_kt, (min(p.Sq, it.q0 + 128) - 1) / 128 + 1);
+  const int b = it.bh / p.Hq, h_q = it.bh % p.Hq;
+  it.bh_kv = b * p.Hkv + h_q / (p.Hq / p.Hkv);
+  return it;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -491,19 +525,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // Head-major (K/V of a head stay hot in L2), heavy query tiles first.
-  const int bh = blockIdx.x / p.n_qt;
-  int qi = blockIdx.x % p.n_qt;
-  if (p.causal) qi = p.n_qt - 1 - qi;
-  const int b = bh / p.Hq, h_q = bh % p.Hq;
-  const int bh_kv = b * p.Hkv + h_q / (p.Hq / p.Hkv);
-  const int q0 = qi * 128;
-  int n_kv = p.n_kt;
-  if (p.causal) n_kv = min(p.n_kt, (min(p.Sq, q0 + 128) - 1) / 128 + 1);
+  const int n_items = p.BHq * p.n_qt;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(QB_Q), 512);
+    mbar_init(bar(QB_QFREE), 1);
+    mbar_init(bar(QB_DQFREE), 512);
     for (int s = 0; s < C::KV_STAGES; ++s) {
       mbar_init(bar(QB_KVFULL + s), 1);
       mbar_init(bar(QB_KVEMPTY + s), 1);
@@ -530,23 +557,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ---------------- TMA producer (whole warp, one elected lane issues) --------
     int issued[C::KV_STAGES] = {};
     bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int st = j % C::KV_STAGES, u = j / C::KV_STAGES;
-      if (u > 0) ok = mbar_wait_warp(bar(QB_KVEMPTY + st), (u - 1) & 1, abort_flag, 501);
-      if (!ok) break;
-      const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
-      if (elect_one()) {
-        mbar_arrive_expect_tx(bar(QB_KVFULL + st), 2 * C::TILE_BYTES);
-        for (int hh = 0; hh < C::HALVES; ++hh) {
-          tma_load_3d(sb + hh * C::HALF_BYTES, &tm_k, bar(QB_KVFULL + st), hh * 64, j * 128,
-                      bh_kv);
-          tma_load_3d(sb + C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v, bar(QB_KVFULL + st),
-                      hh * 64, j * 128, bh_kv);
+    int g = 0;  // K/V tiles this CTA has loaded so far (ring position)
+    for (int k = 0; ok; ++k) {
+      const int w = sched_item(k);
+      if (w >= n_items) break;
+      const DqItem it = dq_item(p, w);
+      for (int j = 0; j < it.n_kv && ok; ++j, ++g) {
+        const int st = g % C::KV_STAGES, u = g / C::KV_STAGES;
+        if (u > 0) ok = mbar_wait_warp(bar(QB_KVEMPTY + st), (u - 1) & 1, abort_flag, 501);
+        if (!ok) break;
+        const uint32_t sb = sbase + C::OFF_STAGE + st * C::STAGE_BYTES;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(bar(QB_KVFULL + st), 2 * C::TILE_BYTES);
+          for (int hh = 0; hh < C::HALVES; ++hh) {
+            tma_load_3d(sb + hh * C::HALF_BYTES, &tm_k, bar(QB_KVFULL + st), hh * 64, j * 128,
+                        it.bh_kv);
+            tma_load_3d(sb + C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v, bar(QB_KVFULL + st),
+                        hh * 64, j * 128, it.bh_kv);
+          }
         }
-      }
-      __syncwarp();
+        __syncwarp();
 #pragma unroll
-      for (int s2 = 0; s2 < C::KV_STAGES; ++s2) issued[s2] += (s2 == st);
+        for (int s2 = 0; s2 < C::KV_STAGES; ++s2) issued[s2] += (s2 == st);
+      }
     }
     if (!ok) {
 #pragma unroll
@@ -561,8 +594,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint64_t d_v0 = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE + C::TILE_BYTES);
     const uint64_t m_k0 = mnmajor_base<C::HALF_BYTES>(sbase + C::OFF_STAGE);
     // S_h = Q K_h^T, dP_h = dO V_h^T for key stage st (A = Q / dO in TMEM),
-    // then signal s_full[h]
-    auto issue_s = [&](int h, int st) {
+    // then signal s_full[h] (and, for the item's last tile, QB_QFREE)
+    auto issue_s = [&](int h, int st, bool last_of_item) {
       if (elect_one()) {
         const uint32_t so = st * C::STAGE_BYTES + h * 64 * 128;
         const uint64_t bk = desc_adv(d_k0, so), bv = desc_adv(d_v0, so);
@@ -576,11 +609,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           mma_ts(ddp, tmem + C::TM_DO + kk * 8, desc_adv(bv, kstep_off(kk, C::HALF_BYTES)),
                  idesc_s, kk > 0);
         tc_commit(bar(QB_SFULL + h));
+        if (last_of_item && h == 1) tc_commit(bar(QB_QFREE));
       }
       __syncwarp();
     };
-    // dQ += dS_h K_h; then an optional commit
-    auto issue_dq = [&](int h, int st, bool acc, int commit) {
+    // dQ += dS_h K_h; then commits
+    auto issue_dq = [&](int h, int st, bool acc, int commit0, int commit1) {
       if (elect_one()) {
         const uint64_t bk = desc_adv(m_k0, st * C::STAGE_BYTES + h * 64 * 128);
         const uint32_t a = tmem + C::tm_s(h);
@@ -588,36 +622,50 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < 4; ++kk)
           mma_ts(tmem + C::TM_DQ, a + packed_col(kk), desc_adv(bk, kk * 16 * 128), idesc_dq,
                  (acc || kk > 0) ? 1u : 0u);
-        if (commit >= 0) tc_commit(bar(commit));
+        if (commit0 >= 0) tc_commit(bar(commit0));
+        if (commit1 >= 0) tc_commit(bar(commit1));
       }
       __syncwarp();
     };
-    bool ok = mbar_wait_warp(bar(QB_Q), 0, abort_flag, 511);
-    if (ok) ok = mbar_wait_warp(bar(QB_KVFULL + 0), 0, abort_flag, 512);
-    if (ok) {
-      tc_fence_after();
-      issue_s(0, 0);
-      issue_s(1, 0);
-    }
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int st = j % C::KV_STAGES;
-      const int stn = (j + 1) % C::KV_STAGES;
-      const bool more = j + 1 < n_kv;
-      ok = mbar_wait_warp(bar(QB_PFULL + 0), j & 1, abort_flag, 513);
+    bool ok = true;
+    int g = 0;
+    for (int li = 0; ok; ++li) {
+      const int w = sched_item(li);
+      if (w >= n_items) break;
+      const DqItem it = dq_item(p, w);
+      ok = mbar_wait_warp(bar(QB_Q), li & 1, abort_flag, 511);  // Q, dO of this item in TMEM
+      if (ok) ok = mbar_wait_warp(bar(QB_KVFULL + g % C::KV_STAGES), (g / C::KV_STAGES) & 1,
+                                  abort_flag, 512);
       if (!ok) break;
       tc_fence_after();
-      issue_dq(0, st, j > 0, -1);
-      if (more) {
-        ok = mbar_wait_warp(bar(QB_KVFULL + stn), ((j + 1) / C::KV_STAGES) & 1, abort_flag, 514);
+      issue_s(0, g % C::KV_STAGES, it.n_kv == 1);
+      issue_s(1, g % C::KV_STAGES, it.n_kv == 1);
+      for (int j = 0; j < it.n_kv && ok; ++j) {
+        const int gj = g + j;
+        const int st = gj % C::KV_STAGES;
+        const int stn = (gj + 1) % C::KV_STAGES;
+        const bool more = j + 1 < it.n_kv;
+        ok = mbar_wait_warp(bar(QB_PFULL + 0), gj & 1, abort_flag, 513);
+        // the previous item's epilogue has read its dQ before this item's
+        // first dQ MMA overwrites the accumulator
+        if (ok && j == 0 && li > 0)
+          ok = mbar_wait_warp(bar(QB_DQFREE), (li - 1) & 1, abort_flag, 517);
         if (!ok) break;
         tc_fence_after();
-        issue_s(0, stn);
+        issue_dq(0, st, j > 0, -1, -1);
+        if (more) {
+          ok = mbar_wait_warp(bar(QB_KVFULL + stn), ((gj + 1) / C::KV_STAGES) & 1, abort_flag, 514);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(0, stn, j + 2 == it.n_kv);
+        }
+        ok = mbar_wait_warp(bar(QB_PFULL + 1), gj & 1, abort_flag, 515);
+        if (!ok) break;
+        tc_fence_after();
+        issue_dq(1, st, true, QB_KVEMPTY + st, more ? -1 : QB_ACC);
+        if (more) issue_s(1, stn, j + 2 == it.n_kv);
       }
-      ok = mbar_wait_warp(bar(QB_PFULL + 1), j & 1, abort_flag, 515);
-      if (!ok) break;
-      tc_fence_after();
-      issue_dq(1, st, true, more ? QB_KVEMPTY + st : QB_ACC);
-      if (more) issue_s(1, stn);
+      g += it.n_kv;
     }
     if (elect_one()) tc_commit(bar(QB_DRAIN));
     __syncwarp();
@@ -630,106 +678,142 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_base = uint32_t(wq * 32) << 16;
-    const int qrow = q0 + row;
-    // Q (warpgroups 0,1) / dO (2,3) row halves into TMEM as the MMAs' A operand.
-    {
-      const __nv_bfloat16* src = (h == 0 ? q : dO) + ((size_t)bh * p.Sq + qrow) * D + cq * (D / 2);
-      const bool in = qrow < p.Sq;
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        uint32_t w[16];
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const uint4 x =
-              in ? reinterpret_cast<const uint4*>(src)[c * 4 + v4] : make_uint4(0, 0, 0, 0);
-          w[4 * v4] = x.x;
-          w[4 * v4 + 1] = x.y;
-          w[4 * v4 + 2] = x.z;
-          w[4 * v4 + 3] = x.w;
-        }
-        tmem_st16(tmem + lane_base + (h == 0 ? C::TM_Q : C::TM_DO) + cq * (D / 4) + c * 16, w);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(QB_Q));
-    }
-    const size_t ws_idx = (size_t)bh * p.Sq_pad + qrow;  // qrow < Sq_pad always
-    const float nlse2 = p.ws_lse2[ws_idx];   // -LSE * log2(e)
-    const float ndelta = p.ws_delta[ws_idx];  // -D
     const float sl2 = p.scale_log2;
     const int col0 = h * 64 + cq * 32;
-    bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      const int kb = j * 128;
-      const bool need_mask = (p.causal && kb + 127 > q0) || (kb + 128 > p.Sk);
-      int lim = p.Sk - 1 - kb;  // key columns with index > lim are hidden
-      if (p.causal) lim = min(lim, qrow - kb);
-      ok = mbar_wait(bar(QB_SFULL + h), j & 1, abort_flag, 521);
-      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
-      if (!ok) break;
-      tc_fence_after();
-      // dS = 2^(s*scale*log2e - lse) * (dP - D), packed to bf16 inside this
-      // warpgroup's own columns (see packed_col), 16 keys per step.
-      auto step = [&](auto mask_tag, int sub) {
-        constexpr bool kMask = decltype(mask_tag)::value;
-        const int c0 = col0 + sub * 16;
-        uint32_t sr[16], dr[16];
-        tmem_ld16(tmem + lane_base + C::tm_s(h) + cq * 32 + sub * 16, sr);
-        tmem_ld16(tmem + lane_base + C::tm_dp(h) + cq * 32 + sub * 16, dr);
-        tmem_wait_ld();
-        uint32_t dsk[8];
+    const __nv_bfloat16* qsrc = h == 0 ? q : dO;
+    // This warpgroup's quarter of the item's Q (h = 0) or dO (h = 1) row:
+    // D/2 elements = D/4 words, prefetched one item ahead.
+    uint32_t pre[D / 4];
+    float pre_nlse2 = 0.0f, pre_ndelta = 0.0f;
+    auto prefetch = [&](int w) {
+      const DqItem it = dq_item(p, w);
+      const int qrow = it.q0 + row;
+      const size_t ws_idx = (size_t)it.bh * p.Sq_pad + qrow;  // qrow < Sq_pad always
+      pre_nlse2 = p.ws_lse2[ws_idx];    // -LSE * log2(e)
+      pre_ndelta = p.ws_delta[ws_idx];  // -D
+      const uint4* src =
+          reinterpret_cast<const uint4*>(qsrc + ((size_t)it.bh * p.Sq + qrow) * D + cq * (D / 2));
+      const bool in = qrow < p.Sq;
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          float p0 = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, nlse2));
-          float p1 = ex2_approx(fmaf(__uint_as_float(sr[i + 1]), sl2, nlse2));
-          if (kMask) {
-            if (c0 + i > lim) p0 = 0.0f;
-            if (c0 + i + 1 > lim) p1 = 0.0f;
-          }
-          dsk[i / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[i]) + ndelta),
-                                   p1 * (__uint_as_float(dr[i + 1]) + ndelta));
-        }
-        tmem_st8(tmem + lane_base + C::tm_s(h) + cq * 32 + sub * 8, dsk);
-      };
-      if (need_mask) {
-        step(std::true_type{}, 0);
-        step(std::true_type{}, 1);
-      } else {
-        step(std::false_type{}, 0);
-        step(std::false_type{}, 1);
+      for (int v4 = 0; v4 < D / 16; ++v4) {
+        const uint4 x = in ? src[v4] : make_uint4(0, 0, 0, 0);
+        pre[4 * v4] = x.x;
+        pre[4 * v4 + 1] = x.y;
+        pre[4 * v4 + 2] = x.z;
+        pre[4 * v4 + 3] = x.w;
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(QB_PFULL + h));
-    }
-    // ---- epilogue: dQ = acc * scale; warpgroup wg writes columns [wg*D/4, (wg+1)*D/4)
-    if (__all_sync(0xffffffffu, ok && mbar_wait(bar(QB_ACC), 0, abort_flag, 522))) {
+    };
+    if (sched_item(0) < n_items) prefetch(sched_item(0));
+    bool ok = true;
+    int g = 0, li = 0;
+    int prev_w = -1;  // item whose epilogue is still owed
+    auto epilogue = [&](int w, int lj) {
+      // dQ = acc * scale; warpgroup wg writes columns [wg*D/4, (wg+1)*D/4)
+      const DqItem it = dq_item(p, w);
+      const int qrow = it.q0 + row;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(QB_ACC), lj & 1, abort_flag, 522))) return false;
       tc_fence_after();
       const bool valid = qrow < p.Sq;
-      __nv_bfloat16* dq_row = p.dq + ((size_t)bh * p.Sq + (valid ? qrow : 0)) * D + wg * (D / 4);
-#pragma unroll 1
-      for (int c = 0; c < D / 128; ++c) {
+      __nv_bfloat16* dq_row = p.dq + ((size_t)it.bh * p.Sq + (valid ? qrow : 0)) * D + wg * (D / 4);
+      if (D / 4 == 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + C::TM_DQ + wg * (D / 4) + c * 32, r);
+        tmem_ld32(tmem + lane_base + C::TM_DQ + wg * (D / 4), r);
         tmem_wait_ld();
-        if (valid) store_row_chunk_bf16(dq_row + c * 32, r, p.scale);
-      }
-      if (D / 4 == 16) {  // D = 64: 16 columns per warpgroup
+        if (valid) store_row_chunk_bf16(dq_row, r, p.scale);
+      } else {  // D = 64: 16 columns per warpgroup
         uint32_t r[16];
         tmem_ld16(tmem + lane_base + C::TM_DQ + wg * (D / 4), r);
         tmem_wait_ld();
         if (valid) {
-          uint32_t w[8];
+          uint32_t wv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            w[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * p.scale,
-                               __uint_as_float(r[2 * i + 1]) * p.scale);
+            wv[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * p.scale,
+                                __uint_as_float(r[2 * i + 1]) * p.scale);
           uint4* d4 = reinterpret_cast<uint4*>(dq_row);
-          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          d4[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          d4[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
         }
       }
+      tc_fence_before();
+      mbar_arrive(bar(QB_DQFREE));
+      return true;
+    };
+    for (; ok; ++li) {
+      const int w = sched_item(li);
+      if (w >= n_items) break;
+      const DqItem it = dq_item(p, w);
+      const int qrow = it.q0 + row;
+      // Stage this item's Q / dO into TMEM once the previous item's S MMAs
+      // have drained, then prefetch the next item's rows.
+      if (li > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(QB_QFREE), (li - 1) & 1, abort_flag, 523));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t wv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) wv[i] = pre[c * 16 + i];
+        tmem_st16(tmem + lane_base + (h == 0 ? C::TM_Q : C::TM_DO) + cq * (D / 4) + c * 16, wv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(QB_Q));
+      const float nlse2 = pre_nlse2, ndelta = pre_ndelta;
+      if (sched_item(li + 1) < n_items) prefetch(sched_item(li + 1));
+      // the previous item's dQ, overlapping this item's first S MMAs
+      if (prev_w >= 0) {
+        ok = epilogue(prev_w, li - 1);
+        if (!ok) break;
+      }
+      for (int j = 0; j < it.n_kv && ok; ++j) {
+        const int gj = g + j;
+        const int kb = j * 128;
+        const bool need_mask = (p.causal && kb + 127 > it.q0) || (kb + 128 > p.Sk);
+        int lim = p.Sk - 1 - kb;  // key columns with index > lim are hidden
+        if (p.causal) lim = min(lim, qrow - kb);
+        ok = mbar_wait(bar(QB_SFULL + h), gj & 1, abort_flag, 521);
+        ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+        if (!ok) break;
+        tc_fence_after();
+        // dS = 2^(s*scale*log2e - lse) * (dP - D), packed to bf16 inside this
+        // warpgroup's own columns (see packed_col), 16 keys per step.
+        auto step = [&](auto mask_tag, int sub) {
+          constexpr bool kMask = decltype(mask_tag)::value;
+          const int c0 = col0 + sub * 16;
+          uint32_t sr[16], dr[16];
+          tmem_ld16(tmem + lane_base + C::tm_s(h) + cq * 32 + sub * 16, sr);
+          tmem_ld16(tmem + lane_base + C::tm_dp(h) + cq * 32 + sub * 16, dr);
+          tmem_wait_ld();
+          uint32_t dsk[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            float p0 = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, nlse2));
+            float p1 = ex2_approx(fmaf(__uint_as_float(sr[i + 1]), sl2, nlse2));
+            if (kMask) {
+              if (c0 + i > lim) p0 = 0.0f;
+              if (c0 + i + 1 > lim) p1 = 0.0f;
+            }
+            dsk[i / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[i]) + ndelta),
+                                     p1 * (__uint_as_float(dr[i + 1]) + ndelta));
+          }
+          tmem_st8(tmem + lane_base + C::tm_s(h) + cq * 32 + sub * 8, dsk);
+        };
+        if (need_mask) {
+          step(std::true_type{}, 0);
+          step(std::true_type{}, 1);
+        } else {
+          step(std::false_type{}, 0);
+          step(std::false_type{}, 1);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(QB_PFULL + h));
+      }
+      g += it.n_kv;
+      prev_w = w;
     }
+    if (ok && prev_w >= 0) epilogue(prev_w, li - 1);
   }
 
   tc_fence_before();

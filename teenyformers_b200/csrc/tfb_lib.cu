@@ -71,15 +71,17 @@ int current_device() {
   return dev;
 }
 
+int g_num_sms[kMaxDevices];
+
 // Raises the dynamic shared-memory limit of every kernel that needs more
-// than 48 KB, once per device.
+// than 48 KB and records the SM count, once per device.
 int ensure_device_setup() {
   static std::once_flag flags[kMaxDevices];
   static int status[kMaxDevices];
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return TF_ERR_CUDA;
   std::call_once(flags[dev], [dev] {
-    cudaError_t e = cudaSuccess;
+    cudaError_t e = cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
     auto set = [&](const void* fn, int bytes) {
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -100,6 +102,13 @@ int ensure_device_setup() {
 }
 
 bool fits_i32(long long v) { return v >= 0 && v <= 0x7fffffffLL; }
+
+// Persistent grids: one CTA per SM (these kernels hold one CTA per SM).
+unsigned persistent_grid(long long items) {
+  const int dev = current_device();
+  const long long sms = (dev >= 0 && dev < kMaxDevices && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
+  return (unsigned)(items < sms ? items : sms);
+}
 
 }  // namespace
 
@@ -253,7 +262,7 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const 
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   const dim3 grid_kv((unsigned)(bhkv * prm.n_kt));
-  const dim3 grid_q((unsigned)(bhq * prm.n_qt));
+  const dim3 grid_q(persistent_grid(bhq * prm.n_qt));
   if (head_dim == 128) {
     fa_bwd_dkdv_sm100_kernel<128><<<grid_kv, BwdKvCfg<128>::kThreads, BwdKvCfg<128>::SMEM_BYTES,
                                     st>>>(tq, tdo, tk, tv, prm);
