@@ -33,6 +33,15 @@ CFG2 = dict(batch=4, seq=2048, heads=32, head_dim=128, rope_base=10000.0)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+def shard_heads(bh: int, world: int, rank: int):
+    """Contiguous range of the B*H heads owned by `rank` (no collective on the
+    data path: attention is independent per head)."""
+    if bh % world != 0:
+        raise ValueError(f"{bh} heads do not split evenly over {world} ranks")
+    per = bh // world
+    return rank * per, (rank + 1) * per
+
+
 def attn_flops(B, H, S, D, causal=True):
     """FA2 convention: fwd 4*B*H*S^2*D (x1/2 causal), bwd = 2.5 x fwd."""
     fwd = 4.0 * B * H * S * S * D * (0.5 if causal else 1.0)
@@ -220,8 +229,8 @@ def main():
     if args.small:
         B = 2
     BH = B * H
-    assert BH % world == 0, "heads must split evenly across ranks"
-    bh_local = BH // world
+    head_lo, head_hi = shard_heads(BH, world, rank)
+    bh_local = head_hi - head_lo
     scale = D ** -0.5
     fwd_flops_total, bwd_flops_total = attn_flops(B, H, S, D, True)
     fwd_flops_rank = fwd_flops_total / world
@@ -294,24 +303,33 @@ def main():
             tfb.rope_transpose(xs[i % n_bufs], CFG2["rope_base"], tfb.TF_ROPE_ROTATE_HALF,
                                out=ys[i % n_bufs])
         n_rope = max(args.steps, 20) * n_bufs
-        re = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(n_rope)]
+        # Capture the launches in a CUDA graph and time one replay: a ~20 us
+        # kernel launched through Python is otherwise timed together with the
+        # host's launch gaps.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(n_rope):
+                tfb.rope_transpose(xs[i % n_bufs], CFG2["rope_base"], tfb.TF_ROPE_ROTATE_HALF,
+                                   out=ys[i % n_bufs])
+        graph.replay()
         barrier()
         torch.cuda.synchronize()
-        for i in range(n_rope):
-            re[i][0].record(stream)
-            tfb.rope_transpose(xs[i % n_bufs], CFG2["rope_base"], tfb.TF_ROPE_ROTATE_HALF,
-                               out=ys[i % n_bufs])
-            re[i][1].record(stream)
+        ra = torch.cuda.Event(enable_timing=True)
+        rb_ = torch.cuda.Event(enable_timing=True)
+        ra.record(stream)
+        graph.replay()
+        rb_.record(stream)
         torch.cuda.synchronize()
         barrier()
-        rope_us = max_over_ranks(sum(a.elapsed_time(b) for a, b in re) / n_rope * 1e3)
+        rope_us = max_over_ranks(ra.elapsed_time(rb_) / n_rope * 1e3)
+        del graph
         rope_bytes = 2 * rb * rs * rh * rd * 2
         rope_gbs = rope_bytes / (rope_us * 1e-6) / 1e9
         rope = {"gbs_per_gpu": rope_gbs, "us_per_launch": rope_us, "bytes_per_launch": rope_bytes,
                 "frac_of_hbm": rope_gbs / peaks["hbm_gbs"],
                 "workload": "config#2 x[4,2048,32,128] bf16 -> RoPE(rotate-half, theta 1e4) -> "
-                            "[4,32,2048,128]; 4 rotating buffer sets (512 MiB) so reads miss L2"}
+                            "[4,32,2048,128]; 4 rotating buffer sets (512 MiB) so reads miss L2; "
+                            f"{n_rope} launches in one CUDA graph replay"}
         del xs, ys
 
     clocks = sampler.stop() if rank == 0 else None

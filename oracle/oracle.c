@@ -26,7 +26,14 @@
  *   orc_transpose_heads   src/kernels/transpose_heads.rs:59-70
  *   orc_merge_heads       src/kernels/transpose_heads.rs:86-95
  *
- * Generalisations (same per-sequence maths, documented in DESIGN.md):
+ * Pinning: RoPE is pinned to the reference's own golden vector
+ * (tests/fixtures/rope, tests/kernel_execution.rs:169-215).  Attention
+ * forward/backward and transpose/merge: parity unpinned against the
+ * reference itself (its kernels cannot be built or run here and its tests
+ * hold no attention fixture); they are cross-checked against a float64
+ * torch witness and numpy instead (tests/test_oracle_pinning.py).
+ *
+ * Generalisations (same per-sequence maths):
  *   - batch: the reference has no batch axis; [B,S,H,D] applies the
  *     reference per b.
  *   - GQA: the reference ignores n_kv_heads; query head h reads KV head
