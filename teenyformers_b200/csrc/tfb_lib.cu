@@ -445,3 +445,56 @@ extern "C" int tf_b200_merge_heads(const void* src, void* dst, int batch, int se
   return launch_transpose(src, dst, batch, seq_len, n_heads, head_dim, elem_bytes, LAYOUT_BHSD,
                           LAYOUT_BSHD, static_cast<cudaStream_t>(stream));
 }
+
+// ===================================================================== backward, no scratch argument
+namespace {
+
+// Scratch for the allocation-free backward: the -LSE*log2(e) and -rowsum(O*dO)
+// rows (2 x 1,048,576 floats = 8 MiB), written in full by every call's prep
+// kernel before use, so nothing needs clearing between calls.
+constexpr size_t kNoAllocWsBytes = size_t(8) << 20;
+__device__ __align__(256) float g_noalloc_ws[kNoAllocWsBytes / sizeof(float)];
+
+// Device address of g_noalloc_ws, looked up once per device with that device
+// current (host code only holds a stand-in symbol for it).
+void* noalloc_workspace(int* status) {
+  static std::once_flag flags[kMaxDevices];
+  static void* ptrs[kMaxDevices];
+  static int statuses[kMaxDevices];
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) {
+    *status = TF_ERR_CUDA;
+    return nullptr;
+  }
+  std::call_once(flags[dev], [dev] {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_ws);
+    ptrs[dev] = e == cudaSuccess ? ptr : nullptr;
+    statuses[dev] = e == cudaSuccess ? TF_OK : TF_ERR_CUDA;
+  });
+  *status = statuses[dev];
+  return ptrs[dev];
+}
+
+}  // namespace
+
+extern "C" int tf_b200_flash_attn2_bwd_bf16_noalloc(const void* q, const void* k, const void* v,
+                                                   const void* o, const void* d_o,
+                                                   const float* lse, void* dq, void* dk, void* dv,
+                                                   int batch, int n_heads_q, int n_heads_kv,
+                                                   int n_ctx_q, int n_ctx_k, int head_dim,
+                                                   float softmax_scale, int causal,
+                                                   void* stream) {
+  if (batch < 0 || n_heads_q < 0 || n_heads_kv < 0 || n_ctx_q < 0 || n_ctx_k < 0)
+    return TF_ERR_INVALID_ARG;
+  if (batch == 0 || n_heads_q == 0 || (n_ctx_q == 0 && n_ctx_k == 0)) return TF_OK;
+  if (n_ctx_q > 0 &&
+      tf_b200_flash_attn2_bwd_workspace_size(batch, n_heads_q, n_ctx_q) > kNoAllocWsBytes)
+    return TF_ERR_TOO_LARGE;
+  int st = TF_OK;
+  void* ws = noalloc_workspace(&st);
+  if (st != TF_OK) return st;
+  return tf_b200_flash_attn2_bwd_bf16(q, k, v, o, d_o, lse, dq, dk, dv, ws, batch, n_heads_q,
+                                      n_heads_kv, n_ctx_q, n_ctx_k, head_dim, softmax_scale,
+                                      causal, stream);
+}
