@@ -5,7 +5,11 @@ Headline workload (BASELINE config #3): causal flash-attention-2 forward +
 backward, bf16, B=8, H=32, S=4096, D=128.  A step is one forward and one
 backward over this rank's share of the B*H heads (strong scaling: the 256
 heads are split across the N ranks with no collective on the data path).
-Also measured: RoPE + head transpose (config #2, [4,2048,32,128] bf16) GB/s.
+Also measured: RoPE + head transpose (config #2, [4,2048,32,128] bf16) GB/s;
+GQA causal forward (config #4, B16 Hq64 Hkv8 S8192, KV groups split across the
+ranks, no collective); the tensor-parallel Llama-3-8B-shaped decoder layer
+prefill (config #5, B4 S4096, heads and FFN split across the ranks with an
+NCCL all-reduce after o_proj and down_proj).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -30,6 +34,9 @@ sys.path.insert(0, ROOT)
 METRIC = "FA2 fwd/bwd TFLOP/s (bf16 causal S4096 D128) at 1/2/4/8 B200; RoPE GB/s"
 CFG3 = dict(batch=8, heads=32, seq=4096, head_dim=128, causal=True)
 CFG2 = dict(batch=4, seq=2048, heads=32, head_dim=128, rope_base=10000.0)
+CFG4 = dict(batch=16, heads_q=64, heads_kv=8, seq=8192, head_dim=128)
+CFG5 = dict(batch=4, seq=4096, d_model=4096, heads=32, kv_heads=8, head_dim=128, d_ff=14336,
+            rope_base=500000.0, eps=1e-5)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -179,6 +186,98 @@ def reference_arm(args, rank, world):
 
 
 # ----------------------------------------------------------------- GPU legs
+def _timed(stream, n, fn):
+    import torch
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n
+
+
+def gqa_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
+    """Config #4: causal GQA forward, the B*Hkv = 128 KV groups (each with its
+    8 query heads) split evenly over the ranks; no collective."""
+    import torch
+
+    import teenyformers_b200 as tfb
+    B, Hq, Hkv, S, D = (CFG4[k] for k in ("batch", "heads_q", "heads_kv", "seq", "head_dim"))
+    if Hkv % world:
+        return {"skipped": f"{Hkv} KV heads do not split over {world} ranks"}
+    hq_l, hkv_l = Hq // world, Hkv // world
+    g = torch.Generator(device=dev).manual_seed(4242 + rank)
+    q = torch.randn((B, hq_l, S, D), generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn((B, hkv_l, S, D), generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn((B, hkv_l, S, D), generator=g, device=dev, dtype=torch.bfloat16)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, hq_l, S), device=dev, dtype=torch.float32)
+    scale = D ** -0.5
+    run = lambda: tfb.flash_attn2_fwd(q, k, v, scale, True, out=o, lse=lse)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        run()
+    n = max(3, min(args.steps, 10))
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(_timed(stream, n, run))
+    barrier()
+    flops = 2.0 * B * Hq * S * S * D  # causal: 4*B*H*S^2*D / 2
+    tf = flops / (ms * 1e-3) / 1e12
+    del q, k, v, o, lse
+    return {"tflops": tf, "tflops_per_gpu": tf / world, "ms_per_step": ms, "steps": n,
+            "frac_of_peak": tf / world / peaks["bf16_tflops_sustained"],
+            "launches": n,
+            "workload": f"config#4 GQA causal fwd B{B} Hq{Hq} Hkv{Hkv} S{S} D{D}; "
+                        f"{hkv_l} KV heads x {B} batches per rank; Q is "
+                        f"{B * hq_l * S * D * 2 / 2**30:.1f} GiB per rank (> L2)"}
+
+
+def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
+    """Config #5: one Llama-3-8B-shaped decoder layer prefill, tensor-parallel
+    over the ranks (NCCL all-reduce after o_proj and down_proj)."""
+    import torch
+    import torch.distributed as dist
+
+    from teenyformers_b200.llama import (LlamaLayerConfig, LlamaLayerTP, init_full_weights,
+                                         shard_weights)
+    c = CFG5
+    cfg = LlamaLayerConfig(d_model=c["d_model"], n_heads=c["heads"], n_kv_heads=c["kv_heads"],
+                           head_dim=c["head_dim"], d_ff=c["d_ff"], rope_base=c["rope_base"],
+                           eps=c["eps"])
+    if cfg.n_kv_heads % world:
+        return {"skipped": f"{cfg.n_kv_heads} KV heads do not split over {world} ranks"}
+    full = init_full_weights(cfg, seed=5, device=dev)
+    w = shard_weights(full, cfg, world, rank)
+    del full
+    ar = (lambda t: dist.all_reduce(t)) if world > 1 else None
+    layer = LlamaLayerTP(cfg, w, world=world, all_reduce=ar)
+    g = torch.Generator(device=dev).manual_seed(55)  # same activations on every rank
+    x = torch.randn((c["batch"], c["seq"], c["d_model"]), generator=g, device=dev,
+                    dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        layer.forward(x)
+    n = max(3, min(args.steps, 10))
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(_timed(stream, n, lambda: layer.forward(x)))
+    barrier()
+    tokens = c["batch"] * c["seq"]
+    flops = cfg.flops(tokens, c["seq"])
+    tf = flops / (ms * 1e-3) / 1e12
+    del layer, w, x
+    return {"tflops": tf, "tokens_per_s": tokens / (ms * 1e-3), "ms_per_step": ms, "steps": n,
+            "flops_per_step": flops, "frac_of_peak": tf / world / peaks["bf16_tflops_sustained"],
+            "launches_per_step_ours": 8,
+            "workload": f"config#5 Llama-3-8B-shaped layer prefill B{c['batch']} S{c['seq']} "
+                        f"d{c['d_model']} H{c['heads']}/{c['kv_heads']} ff{c['d_ff']}, TP x{world}; "
+                        "RMSNorm/RoPE+transpose/attention/merge/SwiGLU on this library's "
+                        "kernels, projections cuBLAS bf16, all-reduce NCCL"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -188,6 +287,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-rope", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-gqa", action="store_true")
+    ap.add_argument("--no-llama", action="store_true")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: 2 of 8 batches (inputs still > L2)")
     args = ap.parse_args()
@@ -332,6 +433,11 @@ def main():
                             f"{n_rope} launches in one CUDA graph replay"}
         del xs, ys
 
+    gqa = None if args.no_gqa else gqa_leg(args, dev, world, rank, barrier, max_over_ranks,
+                                           peaks)
+    llama = None if args.no_llama else llama_leg(args, dev, world, rank, barrier,
+                                                 max_over_ranks, peaks)
+
     clocks = sampler.stop() if rank == 0 else None
 
     # ---- end to end through the public API, host buffers ----
@@ -427,11 +533,15 @@ def main():
                            f"{peaks['bf16_tflops_sustained']}, burst {peaks['bf16_tflops']} "
                            f"TFLOP/s, HBM {peaks['hbm_gbs']} GB/s)",
             "rope": rope,
+            "gqa_fwd": gqa,
+            "llama_layer": llama,
             "rope_gbs": rope["gbs_per_gpu"] if rope else None,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": 4 * args.steps,
+            "gpu_launches_note": "fwd 1 + bwd 3 (prep, dK/dV, dQ) per timed step of the "
+                                 "headline loop; the rope/gqa/llama legs count their own",
             "device_status": status,
         }
         print(json.dumps(line), flush=True)

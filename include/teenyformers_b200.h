@@ -166,6 +166,18 @@ TF_API int tf_b200_transpose_heads(const void* src, void* dst, int batch, int se
 TF_API int tf_b200_merge_heads(const void* src, void* dst, int batch, int seq_len, int n_heads,
                         int head_dim, int elem_bytes, void* stream);
 
+/* ---------------- Llama block row kernels (tensor-parallel layer support) ----------------
+ * RMSNorm with optional fused residual add; replaces the reference's
+ * fused_add_rmsnorm_forward (src/kernels/fused_add_rmsnorm.rs:53-110) and, with
+ * residual == NULL, the teeny-core RmsNorm the layers use (src/layers/mod.rs:61-65):
+ *   h = x + residual (written to h_out if non-NULL), y = h * rsqrt(mean(h^2) + eps) * weight
+ *   x, residual, y, h_out [rows, cols] bf16; weight [cols] bf16; cols % 8 == 0, <= 8192. */
+TF_API int tf_b200_rmsnorm_bf16(const void* x, const void* residual, const void* weight, void* y,
+                                void* h_out, int rows, int cols, float eps, void* stream);
+/* SwiGLU; replaces swiglu_forward (src/kernels/swiglu.rs:56-95):
+ *   z [rows, 2*d_ff] = [gate || up] bf16 -> out[m, n] = silu(gate[m, n]) * up[m, n], [rows, d_ff]. */
+TF_API int tf_b200_swiglu_bf16(const void* z, void* out, int rows, int d_ff, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,8 @@ def _load():
     lib.orc_transpose_heads.argtypes = [P, P, I, I, I, I, I]
     lib.orc_merge_heads.argtypes = [P, P, I, I, I, I, I]
     lib.orc_rope_transpose.argtypes = [P, P, I, I, I, I, F, I, I]
+    lib.orc_rmsnorm.argtypes = [P, P, P, P, P, I, I, F]
+    lib.orc_swiglu.argtypes = [P, P, I, I]
     lib.orc_max_threads.restype = I
     lib.orc_set_threads.argtypes = [I]
     _lib = lib
@@ -154,3 +156,27 @@ def rope_transpose(x, ln_base: float, style: int = ROPE_INTERLEAVED, inverse: bo
     _load().orc_rope_transpose(_ptr(x), _ptr(y), B, S, H, D, float(ln_base), int(style),
                                int(bool(inverse)))
     return y
+
+
+def rmsnorm(x, weight, eps: float, residual=None):
+    """(y, h): h = x + residual (or x), y = h * rsqrt(mean(h^2) + eps) * weight."""
+    x = _f32(x)
+    N = x.shape[-1]
+    M = x.size // N if N else 0
+    w = _f32(weight)
+    r = _f32(residual) if residual is not None else None
+    y = np.empty_like(x)
+    h = np.empty_like(x)
+    _load().orc_rmsnorm(_ptr(x), _ptr(r) if r is not None else None, _ptr(w), _ptr(y), _ptr(h),
+                        M, N, float(eps))
+    return y, h
+
+
+def swiglu(z):
+    """z [..., 2*d_ff] = gate || up -> silu(gate) * up [..., d_ff]."""
+    z = _f32(z)
+    d_ff = z.shape[-1] // 2
+    M = z.size // (2 * d_ff) if d_ff else 0
+    out = np.empty(z.shape[:-1] + (d_ff,), dtype=np.float32)
+    _load().orc_swiglu(_ptr(z), _ptr(out), M, d_ff)
+    return out

@@ -25,9 +25,13 @@
  *                         ln(base) pre-computed by the caller (rope.rs:194).
  *   orc_transpose_heads   src/kernels/transpose_heads.rs:59-70
  *   orc_merge_heads       src/kernels/transpose_heads.rs:86-95
+ *   orc_rmsnorm           src/kernels/fused_add_rmsnorm.rs:53-110 (residual
+ *                         optional: the layers' teeny-core RmsNorm)
+ *   orc_swiglu            src/kernels/swiglu.rs:56-95
  *
- * Pinning: RoPE is pinned to the reference's own golden vector
- * (tests/fixtures/rope, tests/kernel_execution.rs:169-215).  Attention
+ * Pinning: RoPE, RMSNorm and SwiGLU are pinned to the reference's own golden
+ * vectors (tests/fixtures/{rope,fused_add_rmsnorm,swiglu},
+ * tests/kernel_execution.rs:63-215).  Attention
  * forward/backward and transpose/merge: parity unpinned against the
  * reference itself (its kernels cannot be built or run here and its tests
  * hold no attention fixture); they are cross-checked against a float64
@@ -285,4 +289,41 @@ ORC_EXPORT void orc_rope_transpose(const float* x, float* y, int B, int S, int H
         orc_merge_heads(tmp, y, B, S, H, D, 4);
     }
     free(tmp);
+}
+
+/*
+ * Fused residual add + RMSNorm (fused_add_rmsnorm.rs:53-110): h = x + r,
+ * rstd = rsqrt(sum(h^2) / N + eps), y = h * rstd * w.  r may be NULL
+ * (plain RMSNorm); h_out may be NULL.
+ */
+ORC_EXPORT void orc_rmsnorm(const float* x, const float* r, const float* w, float* y,
+                            float* h_out, int M, int N, float eps) {
+#pragma omp parallel for schedule(static)
+    for (long m = 0; m < M; ++m) {
+        const float* xr = x + (size_t)m * N;
+        const float* rr = r ? r + (size_t)m * N : NULL;
+        float ss = 0.0f;
+        for (int n = 0; n < N; ++n) {
+            const float h = xr[n] + (rr ? rr[n] : 0.0f);
+            if (h_out) h_out[(size_t)m * N + n] = h;
+            ss += h * h;
+        }
+        const float rstd = 1.0f / sqrtf(ss * (1.0f / (float)N) + eps);
+        for (int n = 0; n < N; ++n) {
+            const float h = xr[n] + (rr ? rr[n] : 0.0f);
+            y[(size_t)m * N + n] = h * rstd * w[n];
+        }
+    }
+}
+
+/* SwiGLU (swiglu.rs:56-95): z [M, 2*d_ff] = gate || up, out = silu(gate) * up. */
+ORC_EXPORT void orc_swiglu(const float* z, float* out, int M, int d_ff) {
+#pragma omp parallel for schedule(static)
+    for (long m = 0; m < M; ++m)
+        for (int n = 0; n < d_ff; ++n) {
+            const float g = z[(size_t)m * 2 * d_ff + n];
+            const float u = z[(size_t)m * 2 * d_ff + d_ff + n];
+            const float sig = 1.0f / (1.0f + expf(-g));
+            out[(size_t)m * d_ff + n] = g * sig * u;
+        }
 }

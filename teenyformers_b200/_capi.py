@@ -43,6 +43,8 @@ SIGNATURES = {
     "tf_b200_rope_transpose_bf16": (I, [P, P, I, I, I, I, F, I, I, P]),
     "tf_b200_transpose_heads": (I, [P, P, I, I, I, I, I, P]),
     "tf_b200_merge_heads": (I, [P, P, I, I, I, I, I, P]),
+    "tf_b200_rmsnorm_bf16": (I, [P, P, P, P, P, I, I, F, P]),
+    "tf_b200_swiglu_bf16": (I, [P, P, I, I, P]),
 }
 
 

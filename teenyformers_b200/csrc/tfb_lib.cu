@@ -20,6 +20,7 @@
 #include "attn_bwd.cuh"
 #include "attn_f32.cuh"
 #include "rope_transpose.cuh"
+#include "norm_act.cuh"
 
 using namespace tfb;
 
@@ -444,6 +445,49 @@ extern "C" int tf_b200_merge_heads(const void* src, void* dst, int batch, int se
   if (!src || !dst || src == dst) return TF_ERR_INVALID_ARG;
   return launch_transpose(src, dst, batch, seq_len, n_heads, head_dim, elem_bytes, LAYOUT_BHSD,
                           LAYOUT_BSHD, static_cast<cudaStream_t>(stream));
+}
+
+// ===================================================================== Llama-block row kernels
+extern "C" int tf_b200_rmsnorm_bf16(const void* x, const void* residual, const void* weight,
+                                    void* y, void* h_out, int rows, int cols, float eps,
+                                    void* stream) {
+  if (rows < 0 || cols < 0) return TF_ERR_INVALID_ARG;
+  if (rows == 0 || cols == 0) return TF_OK;
+  if (!x || !weight || !y || (h_out && !residual)) return TF_ERR_INVALID_ARG;
+  if (cols % 8 != 0 || cols > 128 * 8 * 8) return TF_ERR_UNSUPPORTED;
+  if (!is_aligned(x, 16) || !is_aligned(weight, 16) || !is_aligned(y, 16) ||
+      (residual && !is_aligned(residual, 16)) || (h_out && !is_aligned(h_out, 16)))
+    return TF_ERR_MISALIGNED;
+  if (!(eps >= 0.0f) || !std::isfinite(eps)) return TF_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const auto* xp = static_cast<const __nv_bfloat16*>(x);
+  const auto* rp = static_cast<const __nv_bfloat16*>(residual);
+  const auto* wp = static_cast<const __nv_bfloat16*>(weight);
+  auto* yp = static_cast<__nv_bfloat16*>(y);
+  auto* hp = static_cast<__nv_bfloat16*>(h_out);
+  const int vpt = (cols / 8 + 127) / 128;
+  if (vpt <= 2)
+    rmsnorm_rows_kernel<2><<<rows, 128, 0, st>>>(xp, rp, wp, yp, hp, cols, eps);
+  else if (vpt <= 4)
+    rmsnorm_rows_kernel<4><<<rows, 128, 0, st>>>(xp, rp, wp, yp, hp, cols, eps);
+  else
+    rmsnorm_rows_kernel<8><<<rows, 128, 0, st>>>(xp, rp, wp, yp, hp, cols, eps);
+  return launch_status();
+}
+
+extern "C" int tf_b200_swiglu_bf16(const void* z, void* out, int rows, int d_ff, void* stream) {
+  if (rows < 0 || d_ff < 0) return TF_ERR_INVALID_ARG;
+  if (rows == 0 || d_ff == 0) return TF_OK;
+  if (!z || !out) return TF_ERR_INVALID_ARG;
+  if (d_ff % 8 != 0) return TF_ERR_UNSUPPORTED;
+  if (!is_aligned(z, 16) || !is_aligned(out, 16)) return TF_ERR_MISALIGNED;
+  const long long total = (long long)rows * (d_ff / 8);
+  const long long blocks = (total + 255) / 256;
+  swiglu_kernel<<<(unsigned)(blocks < 148LL * 16 ? blocks : 148LL * 16), 256, 0,
+                  static_cast<cudaStream_t>(stream)>>>(static_cast<const __nv_bfloat16*>(z),
+                                                       static_cast<__nv_bfloat16*>(out), rows,
+                                                       d_ff);
+  return launch_status();
 }
 
 // ===================================================================== backward, no scratch argument

@@ -29,7 +29,8 @@ from ._capi import TF_ROPE_INTERLEAVED, TF_ROPE_ROTATE_HALF, TfError, call
 __all__ = [
     "FlashAttn2Op", "CausalFlashAttn2Op", "RopeOp", "TransposeHeadsOp", "MergeHeadsOp",
     "flash_attn2_fwd", "flash_attn2_bwd", "rope", "rope_transpose", "transpose_heads",
-    "merge_heads", "bwd_workspace", "TF_ROPE_INTERLEAVED", "TF_ROPE_ROTATE_HALF", "TfError",
+    "merge_heads", "bwd_workspace", "rmsnorm", "swiglu", "TF_ROPE_INTERLEAVED",
+    "TF_ROPE_ROTATE_HALF", "TfError",
 ]
 
 
@@ -165,6 +166,38 @@ def merge_heads(x: torch.Tensor) -> torch.Tensor:
     y = torch.empty((B, S, H * D), dtype=x.dtype, device=x.device)
     call("tf_b200_merge_heads", _ptr(x), _ptr(y), B, S, H, D, x.element_size(), _stream(x))
     return y[0] if x.dim() == 3 else y
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+            residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+            residual_out: torch.Tensor | None = None):
+    """y = h * rsqrt(mean(h^2) + eps) * weight with h = x (+ residual) over the
+    last dim (fused_add_rmsnorm.rs:53-110).  With ``residual`` returns (y, h)."""
+    for t in (x, weight) + ((residual,) if residual is not None else ()):
+        _need(t.is_cuda and t.is_contiguous() and t.dtype == torch.bfloat16,
+              "rmsnorm tensors must be contiguous bf16 CUDA tensors")
+    N = x.shape[-1]
+    _need(weight.numel() == N, "weight must have the last dim's size")
+    rows = x.numel() // max(N, 1)
+    y = torch.empty_like(x) if out is None else out
+    h = None
+    if residual is not None:
+        _need(residual.shape == x.shape, "residual shape mismatch")
+        h = torch.empty_like(x) if residual_out is None else residual_out
+    call("tf_b200_rmsnorm_bf16", _ptr(x), _ptr(residual), _ptr(weight), _ptr(y), _ptr(h), rows,
+         N, float(eps), _stream(x))
+    return (y, h) if residual is not None else y
+
+
+def swiglu(z: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[..., 2*d_ff] = gate || up -> silu(gate) * up (swiglu.rs:56-95)."""
+    _need(z.is_cuda and z.is_contiguous() and z.dtype == torch.bfloat16,
+          "z must be a contiguous bf16 CUDA tensor")
+    d_ff = z.shape[-1] // 2
+    rows = z.numel() // max(2 * d_ff, 1)
+    y = torch.empty(z.shape[:-1] + (d_ff,), dtype=z.dtype, device=z.device) if out is None else out
+    call("tf_b200_swiglu_bf16", _ptr(z), _ptr(y), rows, d_ff, _stream(z))
+    return y
 
 
 # ----------------------------------------------------------------- op classes

@@ -3,12 +3,13 @@
 
 Two kinds of fixture:
 
-1. ``rope_ref/`` -- the reference's OWN RoPE golden vector, copied byte for
-   byte from the teenyformers checkout (``tests/fixtures/rope/{input,output}.bin``
-   and ``meta.json``, produced there by ``tests/fixtures/generate.py:43-79``
-   and checked by ``tests/kernel_execution.rs:169-215`` at abs-tol 1e-4).
-   It pins the oracle's interleaved RoPE.  Needs the reference checkout:
-   ``--reference /path/to/teenyformers``.
+1. ``rope_ref/``, ``swiglu_ref/``, ``fused_add_rmsnorm_ref/`` -- the
+   reference's OWN golden vectors, copied byte for byte from the teenyformers
+   checkout (``tests/fixtures/{rope,swiglu,fused_add_rmsnorm}/``, produced there
+   by ``tests/fixtures/generate.py:43-128`` and checked by
+   ``tests/kernel_execution.rs:63-215`` at abs-tol 1e-4).  They pin the
+   oracle's interleaved RoPE, SwiGLU and fused add + RMSNorm.  Needs the
+   reference checkout: ``--reference /path/to/teenyformers``.
 
 2. ``attn_*.npz`` -- attention known-answer vectors computed by torch in
    float64 with the reference kernel's semantics (top-left causal mask,
@@ -83,19 +84,28 @@ def make_attn():
         print(f"[{name}] written")
 
 
-def copy_reference_rope(reference: str):
-    src = os.path.join(reference, "tests", "fixtures", "rope")
-    dst = os.path.join(HERE, "rope_ref")
-    os.makedirs(dst, exist_ok=True)
-    digests = {}
-    for f in ("input.bin", "output.bin", "meta.json"):
-        shutil.copyfile(os.path.join(src, f), os.path.join(dst, f))
-        with open(os.path.join(dst, f), "rb") as fh:
-            digests[f] = hashlib.sha256(fh.read()).hexdigest()
-    with open(os.path.join(dst, "SOURCE.json"), "w") as fh:
-        json.dump({"copied_from": "teenyformers tests/fixtures/rope (generate.py:43-79)",
-                   "sha256": digests}, fh, indent=2)
-    print(f"[rope_ref] copied from {src}")
+REF_FIXTURES = {
+    "rope": (("input.bin", "output.bin", "meta.json"), "generate.py:43-79"),
+    "swiglu": (("input.bin", "output.bin", "meta.json"), "generate.py:82-101"),
+    "fused_add_rmsnorm": (("input_x.bin", "input_residual.bin", "weight.bin", "output_y.bin",
+                           "output_h.bin", "meta.json"), "generate.py:104-128"),
+}
+
+
+def copy_reference_fixtures(reference: str):
+    for name, (files, where) in REF_FIXTURES.items():
+        src = os.path.join(reference, "tests", "fixtures", name)
+        dst = os.path.join(HERE, name + "_ref")
+        os.makedirs(dst, exist_ok=True)
+        digests = {}
+        for f in files:
+            shutil.copyfile(os.path.join(src, f), os.path.join(dst, f))
+            with open(os.path.join(dst, f), "rb") as fh:
+                digests[f] = hashlib.sha256(fh.read()).hexdigest()
+        with open(os.path.join(dst, "SOURCE.json"), "w") as fh:
+            json.dump({"copied_from": f"teenyformers tests/fixtures/{name} ({where})",
+                       "sha256": digests}, fh, indent=2)
+        print(f"[{name}_ref] copied from {src}")
 
 
 def main():
@@ -103,7 +113,7 @@ def main():
     ap.add_argument("--reference", default=None, help="teenyformers checkout (for rope_ref)")
     args = ap.parse_args()
     if args.reference:
-        copy_reference_rope(args.reference)
+        copy_reference_fixtures(args.reference)
     make_attn()
 
 

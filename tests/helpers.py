@@ -40,3 +40,17 @@ def seeded_normal(shape, seed: int, device="cpu", dtype=torch.bfloat16):
 
 def to_np(t: torch.Tensor) -> np.ndarray:
     return t.detach().float().cpu().numpy()
+
+
+def assert_bf16_close_scaled(name, got, ref, tol=BF16_MAX_ABS, rl2=BF16_REL_L2):
+    """bf16 outputs whose magnitude exceeds 1 (products, residual sums): the
+    max-abs bound applies to |got - ref| / max(1, |ref|), i.e. absolute below
+    1 and relative above (a bf16 output carries 2^-9 relative rounding)."""
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    assert got.shape == ref.shape, f"{name}: shape {got.shape} vs {ref.shape}"
+    assert np.isfinite(got).all(), f"{name}: non-finite values"
+    err = float((np.abs(got - ref) / np.maximum(1.0, np.abs(ref))).max()) if got.size else 0.0
+    r = rel_l2(got, ref) if got.size else 0.0
+    assert err <= tol and r <= rl2, f"{name}: scaled max-abs {err:.3e} (<= {tol}), rel-L2 {r:.3e} (<= {rl2})"
+    return err, r

@@ -104,3 +104,30 @@ def test_oracle_rope_transpose_composes():
     assert np.array_equal(y, ref)
     back = oracle.rope_transpose(y, math.log(500000.0), oracle.ROPE_ROTATE_HALF, inverse=True)
     assert np.abs(back - x).max() < 1e-5
+
+
+def test_oracle_swiglu_matches_reference_fixture():
+    meta = json.load(open(os.path.join(GOLDEN, "swiglu_ref", "meta.json")))
+    m, d_ff = meta["m"], meta["d_ff"]
+    z = np.fromfile(os.path.join(GOLDEN, "swiglu_ref", "input.bin"), dtype="<f4").reshape(m, 2 * d_ff)
+    out = np.fromfile(os.path.join(GOLDEN, "swiglu_ref", "output.bin"), dtype="<f4").reshape(m, d_ff)
+    assert np.abs(oracle.swiglu(z) - out).max() < F32_ABS
+
+
+def test_oracle_fused_add_rmsnorm_matches_reference_fixture():
+    d = os.path.join(GOLDEN, "fused_add_rmsnorm_ref")
+    meta = json.load(open(os.path.join(d, "meta.json")))
+    m, n = meta["m"], meta["n"]
+    rd = lambda f, shape: np.fromfile(os.path.join(d, f), dtype="<f4").reshape(shape)
+    y, h = oracle.rmsnorm(rd("input_x.bin", (m, n)), rd("weight.bin", (n,)), meta["eps"],
+                          residual=rd("input_residual.bin", (m, n)))
+    assert np.abs(y - rd("output_y.bin", (m, n))).max() < F32_ABS
+    assert np.abs(h - rd("output_h.bin", (m, n))).max() < F32_ABS
+
+
+def test_reference_fixture_integrity_all():
+    for name in ("swiglu_ref", "fused_add_rmsnorm_ref"):
+        meta = json.load(open(os.path.join(GOLDEN, name, "SOURCE.json")))
+        for f, digest in meta["sha256"].items():
+            with open(os.path.join(GOLDEN, name, f), "rb") as fh:
+                assert hashlib.sha256(fh.read()).hexdigest() == digest, (name, f)
