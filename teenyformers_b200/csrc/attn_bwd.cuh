@@ -47,22 +47,35 @@
 namespace tfb {
 
 inline long long bwd_sq_pad(int Sq) { return ((long long)Sq + 127) / 128 * 128; }
+// -LSE*log2e and -D rows ([BHq, Sq_pad] fp32 each), as the two-kernel path uses
 inline size_t bwd_workspace_bytes(long long bhq, int Sq) {
   return (size_t)(2 * bhq * bwd_sq_pad(Sq) * 4);
+}
+// ... plus the fused path's fp32 dQ accumulator [BHq, Sq_pad, D] (sized for D = 128)
+inline size_t bwd_fused_workspace_bytes(long long bhq, int Sq) {
+  return bwd_workspace_bytes(bhq, Sq) + (size_t)bhq * bwd_sq_pad(Sq) * 128 * 4;
 }
 
 // ------------------------------------------------------------------ prep
 // grid = ceil(BHq * Sq_pad / 16), block 256: 16 threads per row, 8 elements
 // (16 bytes) each; requires D % 128 == 0 or D == 64.
+// With dq_acc non-null it also zeroes that row of the [rows, D] fp32 dQ
+// accumulator of the fused backward.
 template <int D>
 __global__ void __launch_bounds__(256)
     fa_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
                        const float* __restrict__ lse, float* __restrict__ ws_lse2,
-                       float* __restrict__ ws_delta, int Sq, int Sq_pad, long long rows) {
+                       float* __restrict__ ws_delta, float* __restrict__ dq_acc, int Sq,
+                       int Sq_pad, long long rows) {
   constexpr int TPR = 16;  // threads per row
   const long long row = (long long)blockIdx.x * (256 / TPR) + threadIdx.x / TPR;
   const int sub = threadIdx.x % TPR;
   if (row >= rows) return;
+  if (dq_acc) {
+    float4* z = reinterpret_cast<float4*>(dq_acc + row * D);
+#pragma unroll
+    for (int v = sub; v < D / 4; v += TPR) z[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   const long long bh = row / Sq_pad;
   const int qi = (int)(row % Sq_pad);
   float acc = 0.0f;

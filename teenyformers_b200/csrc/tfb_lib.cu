@@ -18,6 +18,7 @@
 #include "sm100.cuh"
 #include "attn_fwd.cuh"
 #include "attn_bwd.cuh"
+#include "attn_bwd_fused.cuh"
 #include "attn_f32.cuh"
 #include "rope_transpose.cuh"
 #include "norm_act.cuh"
@@ -66,6 +67,22 @@ bool make_bf16_map(CUtensorMap* map, const void* base, int D, int rows, int oute
   return r == CUDA_SUCCESS;
 }
 
+// 2-D fp32 tensor map over the [rows, D] dQ accumulator, (32 x 128) box,
+// 128-byte swizzle (the staging tile the reduction warps write).
+bool make_f32_acc_map(CUtensorMap* map, const void* base, int D, long long rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
+          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
@@ -93,6 +110,8 @@ int ensure_device_setup() {
     set((const void*)fa_bwd_dkdv_sm100_kernel<128>, BwdKvCfg<128>::SMEM_BYTES);
     set((const void*)fa_bwd_dq_sm100_kernel<64>, BwdQCfg<64>::SMEM_BYTES);
     set((const void*)fa_bwd_dq_sm100_kernel<128>, BwdQCfg<128>::SMEM_BYTES);
+    set((const void*)fa_bwd_fused_sm100_kernel<64>, BwdFusedCfg<64>::SMEM_BYTES);
+    set((const void*)fa_bwd_fused_sm100_kernel<128>, BwdFusedCfg<128>::SMEM_BYTES);
     const int f32_max = (3 * kF32Rows + 3 * kF32Tile) * kF32MaxD * 4 + 2 * kF32Tile * 4;
     set((const void*)fa_fwd_f32_kernel, f32_max);
     set((const void*)fa_bwd_dq_f32_kernel, f32_max);
@@ -195,15 +214,18 @@ extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const 
 extern "C" size_t tf_b200_flash_attn2_bwd_workspace_size(int batch, int n_heads_q,
                                                          int n_ctx_q) {
   if (batch <= 0 || n_heads_q <= 0 || n_ctx_q <= 0) return 0;
-  return bwd_workspace_bytes((long long)batch * n_heads_q, n_ctx_q);
+  return bwd_fused_workspace_bytes((long long)batch * n_heads_q, n_ctx_q);
 }
 
-extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const void* v,
-                                            const void* o, const void* d_o, const float* lse,
-                                            void* dq, void* dk, void* dv, void* workspace,
-                                            int batch, int n_heads_q, int n_heads_kv,
-                                            int n_ctx_q, int n_ctx_k, int head_dim,
-                                            float softmax_scale, int causal, void* stream) {
+namespace {
+
+// fused = true: prep (+ accumulator zeroing), fused kernel, dQ conversion;
+// workspace of bwd_fused_workspace_bytes.  fused = false: the deterministic
+// two-kernel path (prep, dK/dV kernel, dQ kernel); bwd_workspace_bytes.
+int bwd_bf16_impl(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                  const float* lse, void* dq, void* dk, void* dv, void* workspace, int batch,
+                  int n_heads_q, int n_heads_kv, int n_ctx_q, int n_ctx_k, int head_dim,
+                  float softmax_scale, int causal, void* stream, bool fused) {
   if (batch < 0 || n_heads_q < 0 || n_heads_kv < 0 || n_ctx_q < 0 || n_ctx_k < 0)
     return TF_ERR_INVALID_ARG;
   if (batch == 0 || n_heads_q == 0 || (n_ctx_q == 0 && n_ctx_k == 0)) return TF_OK;
@@ -228,14 +250,15 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const 
   float* ws_lse2 = static_cast<float*>(workspace);
   float* ws_delta = ws_lse2 + bhq * sq_pad;
   const long long rows = bhq * sq_pad;
+  float* dq_acc = fused ? ws_delta + bhq * sq_pad : nullptr;  // 256-byte aligned
   if (head_dim == 128)
     fa_bwd_prep_kernel<128><<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(d_o), lse,
-        ws_lse2, ws_delta, n_ctx_q, sq_pad, rows);
+        ws_lse2, ws_delta, dq_acc, n_ctx_q, sq_pad, rows);
   else
     fa_bwd_prep_kernel<64><<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(d_o), lse,
-        ws_lse2, ws_delta, n_ctx_q, sq_pad, rows);
+        ws_lse2, ws_delta, dq_acc, n_ctx_q, sq_pad, rows);
   if (int e = launch_status()) return e;
 
   CUtensorMap tq, tdo, tk, tv;
@@ -263,6 +286,26 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const 
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   const dim3 grid_kv((unsigned)(bhkv * prm.n_kt));
+  if (fused) {
+    if (!fits_i32(rows)) return TF_ERR_TOO_LARGE;  // accumulator row index is int
+    CUtensorMap tacc;
+    if (!make_f32_acc_map(&tacc, dq_acc, head_dim, rows)) return TF_ERR_CUDA;
+    const long long out_rows = bhq * (long long)n_ctx_q;
+    const long long groups = out_rows * (head_dim / 8);
+    const unsigned cgrid = (unsigned)std::min<long long>((groups + 255) / 256, 148LL * 16);
+    if (head_dim == 128) {
+      fa_bwd_fused_sm100_kernel<128><<<grid_kv, kFusedThreads, BwdFusedCfg<128>::SMEM_BYTES,
+                                       st>>>(tq, tdo, tk, tv, tacc, prm);
+      fa_bwd_dq_convert_kernel<128><<<cgrid, 256, 0, st>>>(
+          dq_acc, prm.dq, n_ctx_q, sq_pad, out_rows, softmax_scale);
+    } else {
+      fa_bwd_fused_sm100_kernel<64><<<grid_kv, kFusedThreads, BwdFusedCfg<64>::SMEM_BYTES,
+                                      st>>>(tq, tdo, tk, tv, tacc, prm);
+      fa_bwd_dq_convert_kernel<64><<<cgrid, 256, 0, st>>>(
+          dq_acc, prm.dq, n_ctx_q, sq_pad, out_rows, softmax_scale);
+    }
+    return launch_status();
+  }
   const dim3 grid_q(persistent_grid(bhq * prm.n_qt));
   if (head_dim == 128) {
     fa_bwd_dkdv_sm100_kernel<128><<<grid_kv, BwdKvCfg<128>::kThreads, BwdKvCfg<128>::SMEM_BYTES,
@@ -276,6 +319,19 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const 
         tk, tv, prm, static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(d_o));
   }
   return launch_status();
+}
+
+}  // namespace
+
+extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const void* v,
+                                            const void* o, const void* d_o, const float* lse,
+                                            void* dq, void* dk, void* dv, void* workspace,
+                                            int batch, int n_heads_q, int n_heads_kv,
+                                            int n_ctx_q, int n_ctx_k, int head_dim,
+                                            float softmax_scale, int causal, void* stream) {
+  return bwd_bf16_impl(q, k, v, o, d_o, lse, dq, dk, dv, workspace, batch, n_heads_q,
+                       n_heads_kv, n_ctx_q, n_ctx_k, head_dim, softmax_scale, causal, stream,
+                       true);
 }
 
 // ===================================================================== attention fp32
@@ -533,12 +589,12 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16_noalloc(const void* q, const void* k
     return TF_ERR_INVALID_ARG;
   if (batch == 0 || n_heads_q == 0 || (n_ctx_q == 0 && n_ctx_k == 0)) return TF_OK;
   if (n_ctx_q > 0 &&
-      tf_b200_flash_attn2_bwd_workspace_size(batch, n_heads_q, n_ctx_q) > kNoAllocWsBytes)
+      bwd_workspace_bytes((long long)batch * n_heads_q, n_ctx_q) > kNoAllocWsBytes)
     return TF_ERR_TOO_LARGE;
   int st = TF_OK;
   void* ws = noalloc_workspace(&st);
   if (st != TF_OK) return st;
-  return tf_b200_flash_attn2_bwd_bf16(q, k, v, o, d_o, lse, dq, dk, dv, ws, batch, n_heads_q,
-                                      n_heads_kv, n_ctx_q, n_ctx_k, head_dim, softmax_scale,
-                                      causal, stream);
+  // the deterministic two-kernel path: its scratch is only the per-row statistics
+  return bwd_bf16_impl(q, k, v, o, d_o, lse, dq, dk, dv, ws, batch, n_heads_q, n_heads_kv,
+                       n_ctx_q, n_ctx_k, head_dim, softmax_scale, causal, stream, false);
 }
