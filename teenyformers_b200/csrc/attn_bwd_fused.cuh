@@ -43,8 +43,8 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-__device__ __forceinline__ void bulk_wait_group_read0() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_group0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -102,12 +102,14 @@ struct BwdFusedCfg {
   static constexpr int OFF_DO = OFF_Q + 2 * TILE_BYTES;  // 1 stage
   static constexpr int OFF_DS = OFF_DO + TILE_BYTES;  // dS^T [128 keys][128 queries] bf16
   static constexpr int DS_BYTES = 2 * HALF_BYTES;
-  static constexpr int OFF_STG = OFF_DS + DS_BYTES;  // dQ staging [128 rows][32 fp32], SW128
-  static constexpr int STG_BYTES = 128 * 128;
+  static constexpr int OFF_STG = OFF_DS + DS_BYTES;  // 2 x dQ staging [128 rows][32 fp32], SW128
+  static constexpr int STG_BYTES = 2 * 128 * 128;
   static constexpr int OFF_LSE = OFF_STG + STG_BYTES;  // 2 stages x 128 fp32 (-LSE*log2e)
   static constexpr int OFF_DELTA = OFF_LSE + 1024;     // 2 stages x 128 fp32 (-D)
   static constexpr int OFF_BAR = OFF_DELTA + 1024;
-  static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+  // no alignment slack: the dynamic shared window must start 1024-aligned
+  // (checked at kernel entry)
+  static constexpr int SMEM_BYTES = OFF_BAR + 256;
   static constexpr uint32_t TM_ST = 0, TM_DPT = 128, TM_DV = 256, TM_DK = 256 + D;
   static constexpr uint32_t TM_COLS = 512;
 };
@@ -133,10 +135,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                               const __grid_constant__ CUtensorMap tm_v,
                               const __grid_constant__ CUtensorMap tm_dqacc, const BwdParams p) {
   using C = BwdFusedCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
   const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {  // uniform over the CTA: nothing has been set up yet
+    if (threadIdx.x == 0) atomicCAS(&g_device_status, 0, 600);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + FB2_COUNT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -359,14 +364,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (!ok) break;
       tc_fence_after();
       // Phase 1: P^T = 2^(s*scale*log2e - lse), 16 queries per step, packed to
-      // bf16 over columns already read; fp32 P kept for phase 2.
+      // bf16 over columns already read; fp32 P kept for phase 2.  The next
+      // step's TMEM load is in flight while a step computes (the packed
+      // store of step s, columns [8s, 8s+8), never overlaps the load of
+      // step s+1, columns [16s+16, 16s+32)).
       float pf[64];
+      uint32_t sr[2][16];
       auto p_step = [&](auto mask_tag, int sub) {
         constexpr bool kMask = decltype(mask_tag)::value;
         const int c0 = col0 + sub * 16;
-        uint32_t sr[16];
-        tmem_ld16(tmem + lane_base + C::TM_ST + c0, sr);
         tmem_wait_ld();
+        if (sub < 3) tmem_ld16(tmem + lane_base + C::TM_ST + c0 + 16, sr[(sub + 1) & 1]);
+        const uint32_t(&cur)[16] = sr[sub & 1];
         uint32_t pk[8];
 #pragma unroll
         for (int v4 = 0; v4 < 4; ++v4) {
@@ -375,7 +384,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int i = v4 * 4 + e;
-            float pe = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, nl[e]));
+            float pe = ex2_approx(fmaf(__uint_as_float(cur[i]), sl2, nl[e]));
             if (kMask && c0 + i < qlim) pe = 0.0f;
             pf[sub * 16 + i] = pe;
           }
@@ -384,6 +393,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         tmem_st8(tmem + lane_base + C::TM_ST + col0 + sub * 8, pk);
       };
+      tmem_ld16(tmem + lane_base + C::TM_ST + col0, sr[0]);
       if (diag) {
 #pragma unroll
         for (int sub = 0; sub < 4; ++sub) p_step(std::true_type{}, sub);
@@ -399,12 +409,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(bar(FB2_DPFULL), it & 1, abort_flag, 623));
       if (!ok) break;
       tc_fence_after();
+      uint32_t dr[2][16];
+      tmem_ld16(tmem + lane_base + C::TM_DPT + col0, dr[0]);
 #pragma unroll
       for (int sub = 0; sub < 4; ++sub) {
         const int c0 = col0 + sub * 16;
-        uint32_t dr[16];
-        tmem_ld16(tmem + lane_base + C::TM_DPT + c0, dr);
         tmem_wait_ld();
+        if (sub < 3) tmem_ld16(tmem + lane_base + C::TM_DPT + c0 + 16, dr[(sub + 1) & 1]);
+        const uint32_t(&cur)[16] = dr[sub & 1];
         uint32_t dk[8];
 #pragma unroll
         for (int v4 = 0; v4 < 4; ++v4) {
@@ -413,7 +425,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           float dsv[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            dsv[e] = pf[sub * 16 + v4 * 4 + e] * (__uint_as_float(dr[v4 * 4 + e]) + nd[e]);
+            dsv[e] = pf[sub * 16 + v4 * 4 + e] * (__uint_as_float(cur[v4 * 4 + e]) + nd[e]);
           dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
           dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
         }
@@ -474,17 +486,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       mbar_arrive(bar(FB2_DQEMPTY));
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
-        // the previous reduction must have finished reading the staging tile
-        if (threadIdx.x == 0) bulk_wait_group_read0();
+        // chunk c of every tile uses buffer c & 1 (D / 32 chunks per tile is even)
+        const uint32_t buf = uint32_t(c & 1) * (C::STG_BYTES / 2);
+        // the reduction issued two chunks ago (same buffer) must have read it
+        if (threadIdx.x == 0) bulk_wait_group_read1();
         named_bar_sync(1, 128);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          st_shared_v4(stg_row + ((uint32_t(j) ^ uint32_t(row & 7)) << 4), acc[c * 32 + 4 * j],
-                       acc[c * 32 + 4 * j + 1], acc[c * 32 + 4 * j + 2], acc[c * 32 + 4 * j + 3]);
+          st_shared_v4(stg_row + buf + ((uint32_t(j) ^ uint32_t(row & 7)) << 4),
+                       acc[c * 32 + 4 * j], acc[c * 32 + 4 * j + 1], acc[c * 32 + 4 * j + 2],
+                       acc[c * 32 + 4 * j + 3]);
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (threadIdx.x == 0) {
-          tma_reduce_add_2d(&tm_dqacc, sbase + C::OFF_STG, c * 32, grow0);
+          tma_reduce_add_2d(&tm_dqacc, sbase + C::OFF_STG + buf, c * 32, grow0);
           bulk_commit_group();
         }
       }
