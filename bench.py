@@ -507,7 +507,7 @@ def main():
                     "frac_of_burst": fwd_ach / peaks["bf16_tflops"],
                     "traffic": traffic.get("fa_fwd"),
                     "flops_per_launch": fwd_flops_rank, "ms_per_launch": fwd_ms}
-        roof_bwd = {"kernel": "fa_bwd (prep + dK/dV + dQ kernels, one C-ABI call)",
+        roof_bwd = {"kernel": "fa_bwd (prep + fused dK/dV/dQ + dQ convert kernels, one C-ABI call)",
                     "bound": "tensor", "achieved": bwd_ach, "peak": bf16_peak,
                     "unit": "TFLOP/s", "frac": bwd_ach / bf16_peak,
                     "frac_of_burst": bwd_ach / peaks["bf16_tflops"],
@@ -540,7 +540,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": 4 * args.steps,
-            "gpu_launches_note": "fwd 1 + bwd 3 (prep, dK/dV, dQ) per timed step of the "
+            "gpu_launches_note": "fwd 1 + bwd 3 (prep, fused dK/dV/dQ, dQ convert) per timed step of the "
                                  "headline loop; the rope/gqa/llama legs count their own",
             "device_status": status,
         }

@@ -86,7 +86,10 @@ TF_API int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const void
  * reference needs dK/dV zero-initialised for its atomics; this does not).
  * `workspace` is caller-provided scratch of
  * tf_b200_flash_attn2_bwd_workspace_size(...) bytes (per-row softmax
- * statistics); it must stay untouched until the call's work completes. */
+ * statistics and an fp32 dQ accumulator, sized for head_dim <= 128); it must
+ * stay untouched until the call's work completes.  dK/dV are bitwise
+ * repeatable; dQ sums fp32 partials over key tiles in no fixed order (as the
+ * reference's atomics do), so repeats agree to fp32 rounding. */
 TF_API size_t tf_b200_flash_attn2_bwd_workspace_size(int batch, int n_heads_q, int n_ctx_q);
 TF_API int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const void* v, const void* o,
                                  const void* d_o, const float* lse, void* dq, void* dk, void* dv,
@@ -109,7 +112,8 @@ TF_API int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const void
  * Nothing here calls cudaMalloc/cudaFree.  Every call shares the one array,
  * so calls that can overlap on the GPU (different streams) race: serialise
  * them.  Same arguments and results as tf_b200_flash_attn2_bwd_bf16 minus
- * the workspace. */
+ * the workspace; it runs the deterministic two-kernel backward (dQ
+ * recomputed per query tile), so its results are bitwise repeatable. */
 TF_API int tf_b200_flash_attn2_bwd_bf16_noalloc(const void* q, const void* k, const void* v,
                                                const void* o, const void* d_o, const float* lse,
                                                void* dq, void* dk, void* dv, int batch,
