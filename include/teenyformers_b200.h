@@ -121,6 +121,29 @@ TF_API int tf_b200_flash_attn2_bwd_bf16_noalloc(const void* q, const void* k, co
                                                int n_ctx_k, int head_dim, float softmax_scale,
                                                int causal, void* stream);
 
+/* KV-cache decode attention.  No counterpart kernel in the reference: its
+ * generation loop re-runs the whole prefix through the causal op for every
+ * new token (examples/llama_generate.rs:373-400); this is the same softmax
+ * attention (flash_attn2.rs:77-125 semantics) for the new rows only.
+ *   q: [batch, n_heads_q, n_q, head_dim] bf16 (n_q new tokens per sequence)
+ *   k_cache, v_cache: [batch, n_heads_kv, cache_capacity, head_dim] bf16
+ *   cache_seqlens: [batch] int32 on the device, keys held per sequence
+ *     (n_q <= L_b <= cache_capacity; values outside are clamped), the last
+ *     n_q of which are the new tokens': query i sits at position
+ *     L_b - n_q + i and sees keys 0 .. L_b - n_q + i (bottom-right causal).
+ *   o: [batch, n_heads_q, n_q, head_dim] bf16; lse: [batch, n_heads_q, n_q]
+ *     fp32, natural log of the scaled scores' sum.
+ *   workspace: tf_b200_flash_attn2_decode_workspace_size(...) bytes (0 = none
+ *     needed; NULL allowed then), 16-byte aligned.
+ * head_dim 64 or 128; GQA as in the forward. */
+TF_API size_t tf_b200_flash_attn2_decode_workspace_size(int batch, int n_heads_q, int n_heads_kv,
+                                                        int n_q, int cache_capacity, int head_dim);
+TF_API int tf_b200_flash_attn2_decode_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                           void* o, float* lse, const int* cache_seqlens,
+                                           int batch, int n_heads_q, int n_heads_kv, int n_q,
+                                           int cache_capacity, int head_dim, float softmax_scale,
+                                           void* workspace, void* stream);
+
 /* ---------------- flash attention, fp32, reference argument set ----------------
  * Same tensors and argument order as the reference kernels
  * flash_attn2_causal_fwd (flash_attn2.rs:61-72, plus `neg_inf`) and

@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <mutex>
@@ -19,6 +20,7 @@
 #include "attn_fwd.cuh"
 #include "attn_bwd.cuh"
 #include "attn_bwd_fused.cuh"
+#include "attn_decode.cuh"
 #include "attn_f32.cuh"
 #include "rope_transpose.cuh"
 #include "norm_act.cuh"
@@ -112,6 +114,8 @@ int ensure_device_setup() {
     set((const void*)fa_bwd_dq_sm100_kernel<128>, BwdQCfg<128>::SMEM_BYTES);
     set((const void*)fa_bwd_fused_sm100_kernel<64>, BwdFusedCfg<64>::SMEM_BYTES);
     set((const void*)fa_bwd_fused_sm100_kernel<128>, BwdFusedCfg<128>::SMEM_BYTES);
+    set((const void*)fa_decode_kernel<64>, DecCfg<64>::SMEM_BYTES);
+    set((const void*)fa_decode_kernel<128>, DecCfg<128>::SMEM_BYTES);
     const int f32_max = (3 * kF32Rows + 3 * kF32Tile) * kF32MaxD * 4 + 2 * kF32Tile * 4;
     set((const void*)fa_fwd_f32_kernel, f32_max);
     set((const void*)fa_bwd_dq_f32_kernel, f32_max);
@@ -332,6 +336,106 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const 
   return bwd_bf16_impl(q, k, v, o, d_o, lse, dq, dk, dv, workspace, batch, n_heads_q,
                        n_heads_kv, n_ctx_q, n_ctx_k, head_dim, softmax_scale, causal, stream,
                        true);
+}
+
+// ===================================================================== decode
+namespace {
+
+// Key splits of a decode call: enough CTAs for two per SM on a 148-SM part,
+// at least 256 keys (four tiles) per split.  A pure function of the shape, so
+// the workspace query and the launch agree.
+struct DecodeSplit {
+  int row_blocks, splits, chunk;
+};
+DecodeSplit decode_split(int batch, int n_heads_q, int n_heads_kv, int n_q, int cap) {
+  DecodeSplit d;
+  const int G = n_heads_q / n_heads_kv;
+  d.row_blocks = (G * n_q + 15) / 16;
+  const long long base = (long long)batch * n_heads_kv * d.row_blocks;
+  long long want = (2LL * 148 + base - 1) / base;
+  const long long max_splits = std::max<long long>(1, (cap + 255) / 256);
+  want = std::max<long long>(1, std::min(want, max_splits));
+  const long long per = (cap + want - 1) / want;
+  d.chunk = (int)((per + kDecTileKeys - 1) / kDecTileKeys * kDecTileKeys);
+  d.splits = (cap + d.chunk - 1) / d.chunk;
+  return d;
+}
+
+}  // namespace
+
+extern "C" size_t tf_b200_flash_attn2_decode_workspace_size(int batch, int n_heads_q,
+                                                            int n_heads_kv, int n_q,
+                                                            int cache_capacity, int head_dim) {
+  if (batch <= 0 || n_heads_q <= 0 || n_heads_kv <= 0 || n_q <= 0 || cache_capacity <= 0 ||
+      head_dim <= 0 || n_heads_q % n_heads_kv != 0)
+    return 0;
+  const DecodeSplit d = decode_split(batch, n_heads_q, n_heads_kv, n_q, cache_capacity);
+  if (d.splits == 1) return 0;
+  const size_t rows = (size_t)batch * n_heads_q * n_q;
+  return (size_t)d.splits * rows * ((size_t)head_dim + 1) * 4 + 256;
+}
+
+extern "C" int tf_b200_flash_attn2_decode_bf16(const void* q, const void* k_cache,
+                                               const void* v_cache, void* o, float* lse,
+                                               const int* cache_seqlens, int batch,
+                                               int n_heads_q, int n_heads_kv, int n_q,
+                                               int cache_capacity, int head_dim,
+                                               float softmax_scale, void* workspace,
+                                               void* stream) {
+  if (batch < 0 || n_heads_q < 0 || n_heads_kv < 0 || n_q < 0 || cache_capacity < 0)
+    return TF_ERR_INVALID_ARG;
+  if (batch == 0 || n_heads_q == 0 || n_q == 0) return TF_OK;
+  if (n_heads_kv == 0 || cache_capacity < n_q) return TF_ERR_INVALID_ARG;
+  if (n_heads_q % n_heads_kv != 0) return TF_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return TF_ERR_UNSUPPORTED;
+  if (!q || !k_cache || !v_cache || !o || !lse || !cache_seqlens) return TF_ERR_INVALID_ARG;
+  if (!is_aligned(q, 16) || !is_aligned(k_cache, 16) || !is_aligned(v_cache, 16) ||
+      !is_aligned(o, 16) || !is_aligned(lse, 4) || !is_aligned(cache_seqlens, 4))
+    return TF_ERR_MISALIGNED;
+  if (!(softmax_scale > 0.0f) || !std::isfinite(softmax_scale)) return TF_ERR_INVALID_ARG;
+  const long long bhkv = (long long)batch * n_heads_kv;
+  const long long rows = (long long)batch * n_heads_q * n_q;
+  const DecodeSplit d = decode_split(batch, n_heads_q, n_heads_kv, n_q, cache_capacity);
+  if (!fits_i32(bhkv) || !fits_i32(rows * head_dim) || batch > 65535 ||
+      (long long)n_heads_kv * d.row_blocks > 65535)
+    return TF_ERR_TOO_LARGE;
+  if (d.splits > 1 && (!workspace || !is_aligned(workspace, 16))) return TF_ERR_INVALID_ARG;
+  if (int st = ensure_device_setup()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tk, tv;
+  if (!make_bf16_map(&tk, k_cache, head_dim, cache_capacity, (int)bhkv, kDecTileKeys) ||
+      !make_bf16_map(&tv, v_cache, head_dim, cache_capacity, (int)bhkv, kDecTileKeys))
+    return TF_ERR_CUDA;
+  DecodeParams prm;
+  prm.q = static_cast<const __nv_bfloat16*>(q);
+  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.lse = lse;
+  prm.seqlens = cache_seqlens;
+  prm.part_lse = static_cast<float*>(workspace);
+  prm.part_o = d.splits > 1 ? prm.part_lse + (((size_t)d.splits * rows + 63) / 64 * 64) : nullptr;
+  prm.Hq = n_heads_q;
+  prm.Hkv = n_heads_kv;
+  prm.n_q = n_q;
+  prm.cap = cache_capacity;
+  prm.splits = d.splits;
+  prm.chunk = d.chunk;
+  prm.row_blocks = d.row_blocks;
+  prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+  const dim3 grid((unsigned)d.splits, (unsigned)(n_heads_kv * d.row_blocks), (unsigned)batch);
+  if (head_dim == 128)
+    fa_decode_kernel<128><<<grid, kDecThreads, DecCfg<128>::SMEM_BYTES, st>>>(tk, tv, prm);
+  else
+    fa_decode_kernel<64><<<grid, kDecThreads, DecCfg<64>::SMEM_BYTES, st>>>(tk, tv, prm);
+  if (d.splits > 1) {
+    const unsigned cg = (unsigned)((rows + 7) / 8);
+    if (head_dim == 128)
+      fa_decode_combine_kernel<128><<<cg, 256, 0, st>>>(prm.part_o, prm.part_lse, prm.o, lse,
+                                                        rows, d.splits);
+    else
+      fa_decode_combine_kernel<64><<<cg, 256, 0, st>>>(prm.part_o, prm.part_lse, prm.o, lse,
+                                                       rows, d.splits);
+  }
+  return launch_status();
 }
 
 // ===================================================================== attention fp32

@@ -29,7 +29,8 @@ from ._capi import TF_ROPE_INTERLEAVED, TF_ROPE_ROTATE_HALF, TfError, call
 __all__ = [
     "FlashAttn2Op", "CausalFlashAttn2Op", "RopeOp", "TransposeHeadsOp", "MergeHeadsOp",
     "flash_attn2_fwd", "flash_attn2_bwd", "rope", "rope_transpose", "transpose_heads",
-    "merge_heads", "bwd_workspace", "rmsnorm", "swiglu", "TF_ROPE_INTERLEAVED",
+    "merge_heads", "bwd_workspace", "rmsnorm", "swiglu", "flash_attn2_decode",
+    "decode_workspace", "TF_ROPE_INTERLEAVED",
     "TF_ROPE_ROTATE_HALF", "TfError",
 ]
 
@@ -112,6 +113,38 @@ def flash_attn2_bwd(q, k, v, o, lse, do, softmax_scale: float, causal: bool,
     else:
         raise ValueError(f"unsupported dtype {q.dtype}")
     return dq, dk, dv
+
+
+def decode_workspace(q: torch.Tensor, n_heads_kv: int, cache_capacity: int) -> torch.Tensor | None:
+    B, Hq, n_q, D = q.shape
+    n = _capi.raw("tf_b200_flash_attn2_decode_workspace_size", B, Hq, n_heads_kv, n_q,
+                  cache_capacity, D)
+    return torch.empty(int(n), dtype=torch.uint8, device=q.device) if n else None
+
+
+def flash_attn2_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                       cache_seqlens: torch.Tensor, softmax_scale: float,
+                       out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+                       workspace: torch.Tensor | None = None):
+    """KV-cache decode: q [B,Hq,n_q,D], caches [B,Hkv,cap,D], cache_seqlens [B] int32 (device);
+    the last n_q cached keys are the new tokens'.  Returns (o, lse)."""
+    for t in (q, k_cache, v_cache):
+        _need(t.is_cuda and t.is_contiguous() and t.dtype == torch.bfloat16 and t.dim() == 4,
+              "q and the caches must be contiguous 4-D bf16 CUDA tensors")
+    _need(cache_seqlens.is_cuda and cache_seqlens.dtype == torch.int32 and
+          cache_seqlens.is_contiguous(), "cache_seqlens must be a contiguous int32 CUDA tensor")
+    B, Hq, n_q, D = q.shape
+    _, Hkv, cap, Dk = k_cache.shape
+    _need(k_cache.shape == v_cache.shape and k_cache.shape[0] == B and Dk == D,
+          "cache shape mismatch")
+    _need(cache_seqlens.numel() == B, "cache_seqlens must have one entry per sequence")
+    o = torch.empty_like(q) if out is None else out
+    l = torch.empty((B, Hq, n_q), dtype=torch.float32, device=q.device) if lse is None else lse
+    ws = decode_workspace(q, Hkv, cap) if workspace is None else workspace
+    call("tf_b200_flash_attn2_decode_bf16", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(o),
+         _ptr(l), _ptr(cache_seqlens), B, Hq, Hkv, n_q, cap, D, float(softmax_scale), _ptr(ws),
+         _stream(q))
+    return o, l
 
 
 def rope(x: torch.Tensor, rope_base: float, style: int = TF_ROPE_INTERLEAVED,
