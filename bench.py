@@ -35,6 +35,7 @@ METRIC = "FA2 fwd/bwd TFLOP/s (bf16 causal S4096 D128) at 1/2/4/8 B200; RoPE GB/
 CFG3 = dict(batch=8, heads=32, seq=4096, head_dim=128, causal=True)
 CFG2 = dict(batch=4, seq=2048, heads=32, head_dim=128, rope_base=10000.0)
 CFG4 = dict(batch=16, heads_q=64, heads_kv=8, seq=8192, head_dim=128)
+CFG_DEC = dict(batch=64, heads_q=32, heads_kv=8, head_dim=128, cap=4096, min_len=1024, n_q=1)
 CFG5 = dict(batch=4, seq=4096, d_model=4096, heads=32, kv_heads=8, head_dim=128, d_ff=14336,
             rope_base=500000.0, eps=1e-5)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -235,6 +236,65 @@ def gqa_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
                         f"{B * hq_l * S * D * 2 / 2**30:.1f} GiB per rank (> L2)"}
 
 
+def decode_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
+    """KV-cache decode (the next caller of the attention op after prefill):
+    Llama-3-8B attention shape, B=64 sequences with cached lengths uniform in
+    [1024, 4096], one new token each; sequences split evenly over the ranks.
+    HBM-bound: every cached K/V byte is read once."""
+    import numpy as np
+    import torch
+
+    import teenyformers_b200 as tfb
+    c = CFG_DEC
+    if c["batch"] % world:
+        return {"skipped": f"{c['batch']} sequences do not split over {world} ranks"}
+    B = c["batch"] // world
+    Hq, Hkv, D, cap, n_q = c["heads_q"], c["heads_kv"], c["head_dim"], c["cap"], c["n_q"]
+    lens_all = np.random.default_rng(7).integers(c["min_len"], cap + 1, size=c["batch"])
+    lens = lens_all[rank * B:(rank + 1) * B]
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    q = torch.randn((B, Hq, n_q, D), generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn((B, Hkv, cap, D), generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn((B, Hkv, cap, D), generator=g, device=dev, dtype=torch.bfloat16)
+    seq = torch.tensor(lens, dtype=torch.int32, device=dev)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, Hq, n_q), dtype=torch.float32, device=dev)
+    ws = tfb.decode_workspace(q, Hkv, cap)
+    scale = D ** -0.5
+    run = lambda: tfb.flash_attn2_decode(q, k, v, seq, scale, out=o, lse=lse, workspace=ws)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        run()
+    n = max(args.steps, 20)
+    graph = torch.cuda.CUDAGraph()  # ~0.1 ms launches: time them without host gaps
+    with torch.cuda.graph(graph):
+        for _ in range(n):
+            run()
+    graph.replay()
+    barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    us = max_over_ranks(a.elapsed_time(b) / n * 1e3)
+    del graph
+    kv_bytes = int(2 * Hkv * D * 2 * int(lens_all.sum()))
+    qo_bytes = 2 * c["batch"] * Hq * n_q * D * 2
+    gbs = (kv_bytes + qo_bytes) / (us * 1e-6) / 1e9
+    del q, k, v, o
+    return {"gbs": gbs, "gbs_per_gpu": gbs / world, "us_per_step": us, "steps": n,
+            "bytes_per_step": kv_bytes + qo_bytes,
+            "frac_of_hbm": gbs / world / peaks["hbm_gbs"],
+            "workload": f"decode B{c['batch']} Hq{Hq} Hkv{Hkv} D{D} n_q{n_q}, cached lengths "
+                        f"uniform in [{c['min_len']}, {cap}] (seed 7), {B} sequences per rank; "
+                        f"K/V cache {B * Hkv * cap * D * 4 / 2**30:.2f} GiB per rank (> L2); "
+                        f"{n} launches in one CUDA graph replay"}
+
+
 def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
     """Config #5: one Llama-3-8B-shaped decoder layer prefill, tensor-parallel
     over the ranks (NCCL all-reduce after o_proj and down_proj)."""
@@ -289,6 +349,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-gqa", action="store_true")
     ap.add_argument("--no-llama", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: 2 of 8 batches (inputs still > L2)")
     args = ap.parse_args()
@@ -437,6 +498,8 @@ def main():
                                            peaks)
     llama = None if args.no_llama else llama_leg(args, dev, world, rank, barrier,
                                                  max_over_ranks, peaks)
+    decode = None if args.no_decode else decode_leg(args, dev, world, rank, barrier,
+                                                    max_over_ranks, peaks)
 
     clocks = sampler.stop() if rank == 0 else None
 
@@ -535,6 +598,7 @@ def main():
             "rope": rope,
             "gqa_fwd": gqa,
             "llama_layer": llama,
+            "decode": decode,
             "rope_gbs": rope["gbs_per_gpu"] if rope else None,
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -341,8 +341,9 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const 
 // ===================================================================== decode
 namespace {
 
-// Key splits of a decode call: enough CTAs for two per SM on a 148-SM part,
-// at least 256 keys (four tiles) per split.  A pure function of the shape, so
+// Key splits of a decode call: about four CTAs per SM on a 148-SM part (two
+// are resident at a time; smaller units balance varying cache lengths), at
+// least 256 keys (four tiles) per split.  A pure function of the shape, so
 // the workspace query and the launch agree.
 struct DecodeSplit {
   int row_blocks, splits, chunk;
@@ -352,7 +353,7 @@ DecodeSplit decode_split(int batch, int n_heads_q, int n_heads_kv, int n_q, int 
   const int G = n_heads_q / n_heads_kv;
   d.row_blocks = (G * n_q + 15) / 16;
   const long long base = (long long)batch * n_heads_kv * d.row_blocks;
-  long long want = (2LL * 148 + base - 1) / base;
+  long long want = (4LL * 148 + base - 1) / base;
   const long long max_splits = std::max<long long>(1, (cap + 255) / 256);
   want = std::max<long long>(1, std::min(want, max_splits));
   const long long per = (cap + want - 1) / want;
