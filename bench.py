@@ -295,6 +295,12 @@ def decode_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
                         f"{n} launches in one CUDA graph replay"}
 
 
+def tfb_status() -> int:
+    """The library's device status word (0 unless a bounded device wait expired); cleared."""
+    import teenyformers_b200 as tfb
+    return tfb.device_status(clear=True)
+
+
 def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
     """Config #5: one Llama-3-8B-shaped decoder layer prefill, tensor-parallel
     over the ranks (NCCL all-reduce after o_proj and down_proj)."""
@@ -312,30 +318,51 @@ def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
     full = init_full_weights(cfg, seed=5, device=dev)
     w = shard_weights(full, cfg, world, rank)
     del full
-    ar = (lambda t: dist.all_reduce(t)) if world > 1 else None
-    layer = LlamaLayerTP(cfg, w, world=world, all_reduce=ar)
     g = torch.Generator(device=dev).manual_seed(55)  # same activations on every rank
     x = torch.randn((c["batch"], c["seq"], c["d_model"]), generator=g, device=dev,
                     dtype=torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
-        layer.forward(x)
-    n = max(3, min(args.steps, 10))
-    barrier()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(_timed(stream, n, lambda: layer.forward(x)))
-    barrier()
     tokens = c["batch"] * c["seq"]
     flops = cfg.flops(tokens, c["seq"])
+    n = max(3, min(args.steps, 10))
+
+    def measure(layer):
+        for _ in range(args.warmup):
+            layer.forward(x)
+        barrier()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(_timed(stream, n, lambda: layer.forward(x)))
+        barrier()
+        return ms
+
+    res = {}
+    if world > 1:
+        from teenyformers_b200.tp import PeerAllReduceNorm
+        peer = PeerAllReduceNorm(tokens, c["d_model"], device=dev)
+        ms_nccl = measure(LlamaLayerTP(cfg, w, world=world,
+                                       all_reduce=lambda t: dist.all_reduce(t)))
+        ms = measure(LlamaLayerTP(cfg, w, world=world, peer_ar=peer))
+        res["nccl_allreduce_ms_per_step"] = ms_nccl
+        res["nccl_allreduce_tflops"] = flops / (ms_nccl * 1e-3) / 1e12
+        collective = ("all-reduce + residual + RMSNorm fused in one kernel over NVLink peer "
+                      "memory (this library); nccl_* = the same layer with NCCL all-reduces")
+        launches = 8
+    else:
+        ms = measure(LlamaLayerTP(cfg, w, world=world))
+        collective = "no collective at TP x1"
+        launches = 8
     tf = flops / (ms * 1e-3) / 1e12
-    del layer, w, x
-    return {"tflops": tf, "tokens_per_s": tokens / (ms * 1e-3), "ms_per_step": ms, "steps": n,
-            "flops_per_step": flops, "frac_of_peak": tf / world / peaks["bf16_tflops_sustained"],
-            "launches_per_step_ours": 8,
-            "workload": f"config#5 Llama-3-8B-shaped layer prefill B{c['batch']} S{c['seq']} "
-                        f"d{c['d_model']} H{c['heads']}/{c['kv_heads']} ff{c['d_ff']}, TP x{world}; "
-                        "RMSNorm/RoPE+transpose/attention/merge/SwiGLU on this library's "
-                        "kernels, projections cuBLAS bf16, all-reduce NCCL"}
+    del w, x
+    res["device_status"] = tfb_status()
+    res.update({"tflops": tf, "tokens_per_s": tokens / (ms * 1e-3), "ms_per_step": ms,
+                "steps": n, "flops_per_step": flops,
+                "frac_of_peak": tf / world / peaks["bf16_tflops_sustained"],
+                "launches_per_step_ours": launches,
+                "workload": f"config#5 Llama-3-8B-shaped layer prefill B{c['batch']} S{c['seq']} "
+                            f"d{c['d_model']} H{c['heads']}/{c['kv_heads']} ff{c['d_ff']}, "
+                            f"TP x{world}; RMSNorm/RoPE+transpose/attention/merge/SwiGLU on this "
+                            "library's kernels, projections cuBLAS bf16; " + collective})
+    return res
 
 
 def main():

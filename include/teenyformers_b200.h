@@ -144,6 +144,28 @@ TF_API int tf_b200_flash_attn2_decode_bf16(const void* q, const void* k_cache, c
                                            int cache_capacity, int head_dim, float softmax_scale,
                                            void* workspace, void* stream);
 
+/* Tensor-parallel all-reduce fused with the residual add and RMSNorm after it.
+ * No counterpart in the reference (its layer is single-device); it stands for
+ * "sum the ranks' partial o_proj / down_proj outputs, then fused add + RMSNorm"
+ * (src/layers/llama_block.rs:55-65, fused_add_rmsnorm.rs:53-110) in one kernel
+ * over NVLink peer memory.
+ *   peer_src, peer_h, peer_signal: DEVICE arrays of `world` pointers to every
+ *     rank's [rows, cols] bf16 partial, [rows, cols] bf16 h buffer and signal
+ *     pad (at least 9216 bytes, zeroed once before the first call) -- peer-
+ *     mapped (symmetric) memory, e.g. torch.distributed._symmetric_memory.
+ *   residual: [rows, cols] bf16, identical on every rank, or NULL.
+ *   h (every rank's h buffer) = residual + sum of the partials (bf16);
+ *   y = RMSNorm(h) * weight, local, when weight/y are non-NULL.
+ *   epoch: 1, 2, 3, ... one per call, the same on every rank.
+ * Every rank calls it with the same arguments (own rank); rows % world == 0,
+ * cols % 8 == 0, world <= 8.  Its waits on peers are bounded: on expiry it sets
+ * tf_b200_device_status and the outputs are invalid. */
+TF_API int tf_b200_allreduce_residual_rmsnorm_bf16(const void* const* peer_src, void* const* peer_h,
+                                                  void* const* peer_signal, const void* residual,
+                                                  const void* weight, void* y, int rank, int world,
+                                                  int rows, int cols, float eps, unsigned epoch,
+                                                  void* stream);
+
 /* ---------------- flash attention, fp32, reference argument set ----------------
  * Same tensors and argument order as the reference kernels
  * flash_attn2_causal_fwd (flash_attn2.rs:61-72, plus `neg_inf`) and

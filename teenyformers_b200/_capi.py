@@ -38,6 +38,7 @@ SIGNATURES = {
     "tf_b200_flash_attn2_bwd_bf16_noalloc": (I, [P] * 9 + [I, I, I, I, I, I, F, I, P]),
     "tf_b200_flash_attn2_decode_workspace_size": (SZ, [I] * 6),
     "tf_b200_flash_attn2_decode_bf16": (I, [P] * 6 + [I] * 6 + [F, P, P]),
+    "tf_b200_allreduce_residual_rmsnorm_bf16": (I, [P] * 6 + [I] * 4 + [F, ctypes.c_uint, P]),
     "tf_b200_flash_attn2_fwd_f32": (I, [P, P, P, P, P, I, I, I, I, F, F, I, P]),
     "tf_b200_flash_attn2_bwd_f32": (I, [P] * 9 + [I, I, I, I, F, I, P]),
     "tf_b200_rope_f32": (I, [P, P, I, I, I, F, I, I, P]),

@@ -24,6 +24,7 @@
 #include "attn_f32.cuh"
 #include "rope_transpose.cuh"
 #include "norm_act.cuh"
+#include "comm_norm.cuh"
 
 using namespace tfb;
 
@@ -633,6 +634,36 @@ extern "C" int tf_b200_rmsnorm_bf16(const void* x, const void* residual, const v
     rmsnorm_rows_kernel<4><<<rows, 128, 0, st>>>(xp, rp, wp, yp, hp, cols, eps);
   else
     rmsnorm_rows_kernel<8><<<rows, 128, 0, st>>>(xp, rp, wp, yp, hp, cols, eps);
+  return launch_status();
+}
+
+extern "C" int tf_b200_allreduce_residual_rmsnorm_bf16(
+    const void* const* peer_src, void* const* peer_h, void* const* peer_signal,
+    const void* residual, const void* weight, void* y, int rank, int world, int rows, int cols,
+    float eps, unsigned epoch, void* stream) {
+  if (rows < 0 || cols < 0 || world < 1 || world > kArMaxWorld || rank < 0 || rank >= world)
+    return TF_ERR_INVALID_ARG;
+  if (rows == 0 || cols == 0) return TF_OK;
+  if (!peer_src || !peer_h || !peer_signal) return TF_ERR_INVALID_ARG;
+  if ((weight == nullptr) != (y == nullptr)) return TF_ERR_INVALID_ARG;
+  if (rows % world != 0 || cols % 8 != 0) return TF_ERR_UNSUPPORTED;
+  if (!is_aligned(residual, 16) || !is_aligned(weight, 16) || !is_aligned(y, 16))
+    return TF_ERR_MISALIGNED;
+  if (epoch == 0) return TF_ERR_INVALID_ARG;  // flags start at 0: epochs count from 1
+  auto launch = [&](auto kernel) {
+    kernel<<<kArCtas, kArThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16* const*>(peer_src),
+        reinterpret_cast<__nv_bfloat16* const*>(peer_h),
+        reinterpret_cast<uint32_t* const*>(peer_signal), static_cast<const __nv_bfloat16*>(residual),
+        static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(y), rank, world, rows,
+        cols, eps, epoch);
+  };
+  if (world <= 2)
+    launch(allreduce_residual_rmsnorm_kernel<2>);
+  else if (world <= 4)
+    launch(allreduce_residual_rmsnorm_kernel<4>);
+  else
+    launch(allreduce_residual_rmsnorm_kernel<8>);
   return launch_status();
 }
 

@@ -17,7 +17,10 @@ heads and d_ff/N FFN columns, so the only exchange is an all-reduce (sum) of
 the o_proj and down_proj partial outputs.  The attention pieces, RoPE +
 transpose, merge, RMSNorm (fused with the residual add) and SwiGLU run on
 this library's sm_100a kernels; the projections are plain bf16 GEMMs
-(torch.matmul -> cuBLAS).  The all-reduce is NCCL through torch.distributed.
+(torch.matmul -> cuBLAS).  The all-reduce is either NCCL through
+torch.distributed (`all_reduce`) or, with `peer_ar` (a tp.PeerAllReduceNorm),
+this library's kernel that does the all-reduce, the residual add and the
+RMSNorm in one pass over NVLink peer memory.
 """
 from __future__ import annotations
 
@@ -100,7 +103,8 @@ class LlamaLayerTP:
     """One decoder layer on this rank's shard; `all_reduce` sums a tensor over
     the tensor-parallel group in place (identity for one rank)."""
 
-    def __init__(self, cfg: LlamaLayerConfig, weights: dict, world: int = 1, all_reduce=None):
+    def __init__(self, cfg: LlamaLayerConfig, weights: dict, world: int = 1, all_reduce=None,
+                 peer_ar=None):
         if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.d_ff % world:
             raise ValueError("heads and d_ff must split evenly over the ranks")
         self.cfg = cfg
@@ -110,6 +114,7 @@ class LlamaLayerTP:
         self.hkv = cfg.n_kv_heads // world
         self.ff = cfg.d_ff // world
         self.all_reduce = all_reduce or (lambda t: t)
+        self.peer_ar = peer_ar
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -124,6 +129,16 @@ class LlamaLayerTP:
         k = ops.rope_transpose(k.view(B, S, self.hkv, D), cfg.rope_base, cfg.rope_style)
         v = ops.transpose_heads(v, self.hkv)
         o, _ = ops.flash_attn2_fwd(q, k, v, self.scale, True)
+        if self.peer_ar is not None:
+            # partials straight into the symmetric buffer; all-reduce + residual
+            # + RMSNorm in one kernel; the layer output is the second h buffer
+            ar = self.peer_ar
+            torch.matmul(ops.merge_heads(o), w["wo"].t(), out=ar.part.view(B, S, d))
+            x2, h2 = ar(0, x, w["norm2"], cfg.eps)
+            a = ops.swiglu(torch.matmul(h2.view(B, S, d), w["w_gate_up"].t()))
+            torch.matmul(a, w["w_down"].t(), out=ar.part.view(B, S, d))
+            out, _ = ar(1, x2)
+            return out.view(B, S, d)
         attn = torch.matmul(ops.merge_heads(o), w["wo"].t())
         self.all_reduce(attn)
         h2, x2 = ops.rmsnorm(attn, w["norm2"], cfg.eps, residual=x)
