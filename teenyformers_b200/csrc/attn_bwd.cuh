@@ -52,24 +52,27 @@ inline size_t bwd_workspace_bytes(long long bhq, int Sq) {
   return (size_t)(2 * bhq * bwd_sq_pad(Sq) * 4);
 }
 // ... plus the fused path's fp32 dQ accumulator [BHq, Sq_pad, D] (sized for D = 128)
+// and its work-item counter (256 bytes)
 inline size_t bwd_fused_workspace_bytes(long long bhq, int Sq) {
-  return bwd_workspace_bytes(bhq, Sq) + (size_t)bhq * bwd_sq_pad(Sq) * 128 * 4;
+  return bwd_workspace_bytes(bhq, Sq) + (size_t)bhq * bwd_sq_pad(Sq) * 128 * 4 + 256;
 }
 
 // ------------------------------------------------------------------ prep
 // grid = ceil(BHq * Sq_pad / 16), block 256: 16 threads per row, 8 elements
 // (16 bytes) each; requires D % 128 == 0 or D == 64.
 // With dq_acc non-null it also zeroes that row of the [rows, D] fp32 dQ
-// accumulator of the fused backward.
+// accumulator of the fused backward, and with counter non-null resets the
+// fused kernel's work-item counter.
 template <int D>
 __global__ void __launch_bounds__(256)
     fa_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
                        const float* __restrict__ lse, float* __restrict__ ws_lse2,
-                       float* __restrict__ ws_delta, float* __restrict__ dq_acc, int Sq,
-                       int Sq_pad, long long rows) {
+                       float* __restrict__ ws_delta, float* __restrict__ dq_acc,
+                       int* __restrict__ counter, int Sq, int Sq_pad, long long rows) {
   constexpr int TPR = 16;  // threads per row
   const long long row = (long long)blockIdx.x * (256 / TPR) + threadIdx.x / TPR;
   const int sub = threadIdx.x % TPR;
+  if (counter && blockIdx.x == 0 && threadIdx.x == 0) *counter = 0;
   if (row >= rows) return;
   if (dq_acc) {
     float4* z = reinterpret_cast<float4*>(dq_acc + row * D);
@@ -115,6 +118,8 @@ struct BwdParams {
   float scale;       // softmax scale (natural)
   float scale_log2;  // scale * log2(e)
   int causal;
+  int* work_counter;  // fused path: next work item (zeroed by the prep kernel)
+  int n_items;        // fused path: BHkv * n_kt
 };
 
 __device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, uint32_t bytes,

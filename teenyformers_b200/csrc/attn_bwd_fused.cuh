@@ -115,10 +115,13 @@ struct BwdFusedCfg {
 };
 
 enum BwdFusedBar {
-  FB2_KV = 0, FB2_QFULL = 1, FB2_QEMPTY = 3, FB2_DOFULL = 5, FB2_DOEMPTY = 6, FB2_SFULL = 7,
-  FB2_PFULL = 8, FB2_DPFULL = 9, FB2_DSFULL = 10, FB2_DQFULL = 11, FB2_DQEMPTY = 12,
-  FB2_ACC = 13, FB2_DRAIN = 14, FB2_COUNT = 15
+  FB2_KVFULL = 0, FB2_KVEMPTY = 1, FB2_QFULL = 2, FB2_QEMPTY = 4, FB2_DOFULL = 6,
+  FB2_DOEMPTY = 7, FB2_SFULL = 8, FB2_PFULL = 9, FB2_DPFULL = 10, FB2_DSFULL = 11,
+  FB2_DQFULL = 12, FB2_DQEMPTY = 13, FB2_ACC = 14, FB2_ACCFREE = 15, FB2_ITEMFULL = 16,
+  FB2_ITEMEMPTY = 20, FB2_DRAIN = 24, FB2_COUNT = 25
 };
+constexpr int kItemRing = 4;      // work items the TMA warp may fetch ahead
+constexpr int kItemConsumers = 13;  // MMA warp + 8 elementwise warps + 4 reduction warps
 
 // TMEM column (relative to the operand's base) of the bf16-packed P^T / dS^T
 // for the 16-query K step kk: elementwise warpgroup e packs its 64 query
@@ -127,6 +130,31 @@ __device__ __forceinline__ constexpr uint32_t packed_col64(int kk) {
   return uint32_t((kk >> 2) * 64 + (kk & 3) * 8);
 }
 
+// Work item w = one 128-key tile of one KV head, head-major (a head's Q/dO
+// stay hot in L2 while its key tiles run), key tile 0 first within a head
+// (the most query tiles when causal).
+struct FusedItem {
+  int bh_kv, b, hk, k0, qt_first, qt_per_head, n_tiles;
+};
+__device__ __forceinline__ FusedItem fused_item(const BwdParams& p, int w) {
+  FusedItem it;
+  it.bh_kv = w / p.n_kt;
+  const int kt = w % p.n_kt;
+  it.b = it.bh_kv / p.Hkv;
+  it.hk = it.bh_kv % p.Hkv;
+  it.k0 = kt * 128;
+  it.qt_first = p.causal ? min(kt, p.n_qt) : 0;  // query tile i sees keys iff i >= kt
+  it.qt_per_head = p.n_qt - it.qt_first;
+  it.n_tiles = (p.Hq / p.Hkv) * it.qt_per_head;
+  return it;
+}
+
+// Persistent: one CTA per SM takes work items from a global counter (zeroed
+// by the prep kernel); the TMA warp fetches them into a small shared ring the
+// other roles read.  Tile-level barriers run on a CTA-wide tile count across
+// items; per item, the next item's K/V load and first S^T / dP^T MMAs overlap
+// the previous item's dK/dV epilogue (its first dV/dK MMA waits until the
+// epilogue has read the accumulators out of TMEM).
 template <int D>
 __global__ void __launch_bounds__(kFusedThreads, 1)
     fa_bwd_fused_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -145,21 +173,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + FB2_COUNT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* item_ring = reinterpret_cast<volatile int*>(tmem_slot + 2);
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // Head-major; within a head key tile 0 first (most query tiles when causal).
-  const int bh_kv = blockIdx.x / p.n_kt;
-  const int kt = blockIdx.x % p.n_kt;
-  const int b = bh_kv / p.Hkv, hk = bh_kv % p.Hkv;
   const int G = p.Hq / p.Hkv;
-  const int k0 = kt * 128;
-  const int qt_first = p.causal ? min(kt, p.n_qt) : 0;  // query tile i sees keys iff i >= kt
-  const int qt_per_head = p.n_qt - qt_first;
-  const int n_tiles = G * qt_per_head;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(FB2_KV), 1);
+    mbar_init(bar(FB2_KVFULL), 1);
+    mbar_init(bar(FB2_KVEMPTY), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(FB2_QFULL + s), 1);
       mbar_init(bar(FB2_QEMPTY + s), 1);
@@ -173,6 +194,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     mbar_init(bar(FB2_DQFULL), 1);
     mbar_init(bar(FB2_DQEMPTY), 128);
     mbar_init(bar(FB2_ACC), 1);
+    mbar_init(bar(FB2_ACCFREE), 256);
+    for (int s = 0; s < kItemRing; ++s) {
+      mbar_init(bar(FB2_ITEMFULL + s), 1);
+      mbar_init(bar(FB2_ITEMEMPTY + s), kItemConsumers);
+    }
     mbar_init(bar(FB2_DRAIN), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -186,62 +212,97 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Item k of this CTA, read by a consumer warp from the ring (-1: no more);
+  // false when the wait gave up.
+  auto take_item = [&](int k, int& w) -> bool {
+    const int slot = k % kItemRing;
+    if (!mbar_wait_warp(bar(FB2_ITEMFULL + slot), (k / kItemRing) & 1, abort_flag, 640))
+      return false;
+    w = item_ring[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(FB2_ITEMEMPTY + slot));
+    return true;
+  };
+
   if (warp >= kFusedMmaWarp) {
     if constexpr (D == 128) regs_dec<kRegsProducer>();
-    if (warp == kFusedTmaWarp && n_tiles > 0) {
-      // ---------------- TMA producer (whole warp, one elected lane issues) ------
-      int issued_q[2] = {0, 0}, issued_do = 0;
+    if (warp == kFusedTmaWarp) {
+      // ---------------- TMA producer: fetches the items, loads K/V, Q, dO ------
+      int kv_loads = 0, issued_q[2] = {0, 0}, issued_do = 0, g = 0;
       bool ok = true;
-      if (elect_one()) {
-        mbar_arrive_expect_tx(bar(FB2_KV), 2 * C::TILE_BYTES);
-        for (int hh = 0; hh < C::HALVES; ++hh) {
-          tma_load_3d(sbase + C::OFF_K + hh * C::HALF_BYTES, &tm_k, bar(FB2_KV), hh * 64, k0,
-                      bh_kv);
-          tma_load_3d(sbase + C::OFF_V + hh * C::HALF_BYTES, &tm_v, bar(FB2_KV), hh * 64, k0,
-                      bh_kv);
+      for (int k = 0; ok; ++k) {
+        const int slot = k % kItemRing;
+        if (k >= kItemRing)
+          ok = mbar_wait_warp(bar(FB2_ITEMEMPTY + slot), ((k / kItemRing) - 1) & 1, abort_flag,
+                              601);
+        if (!ok) break;
+        int w = 0;
+        if (lane == 0) {
+          w = k == 0 ? (int)blockIdx.x : atomicAdd(p.work_counter, 1) + (int)gridDim.x;
+          if (w >= p.n_items) w = -1;
+          item_ring[slot] = w;
         }
-      }
-      __syncwarp();
-      for (int it = 0; it < n_tiles && ok; ++it) {
-        const int st = it & 1, u = it >> 1;
-        const int g = it / qt_per_head;
-        const int qi = qt_first + it % qt_per_head;
-        const int bh_q = b * p.Hq + hk * G + g;
-        // Q (+ -LSE*log2e, -D) into stage st
-        if (u > 0) ok = mbar_wait_warp(bar(FB2_QEMPTY + st), (u - 1) & 1, abort_flag, 601);
+        w = __shfl_sync(0xffffffffu, w, 0);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(FB2_ITEMFULL + slot));
+        if (w < 0) break;
+        const FusedItem it = fused_item(p, w);
+        if (it.n_tiles == 0) continue;
+        if (kv_loads > 0)
+          ok = mbar_wait_warp(bar(FB2_KVEMPTY), (kv_loads - 1) & 1, abort_flag, 602);
         if (!ok) break;
         if (elect_one()) {
-          const uint32_t sq = sbase + C::OFF_Q + st * C::TILE_BYTES;
-          mbar_arrive_expect_tx(bar(FB2_QFULL + st), C::TILE_BYTES + 1024);
-          for (int hh = 0; hh < C::HALVES; ++hh)
-            tma_load_3d(sq + hh * C::HALF_BYTES, &tm_q, bar(FB2_QFULL + st), hh * 64, qi * 128,
-                        bh_q);
-          const size_t ws_off = (size_t)bh_q * p.Sq_pad + (size_t)qi * 128;
-          bulk_load(sbase + C::OFF_LSE + st * 512, p.ws_lse2 + ws_off, 512, bar(FB2_QFULL + st));
-          bulk_load(sbase + C::OFF_DELTA + st * 512, p.ws_delta + ws_off, 512,
-                    bar(FB2_QFULL + st));
+          mbar_arrive_expect_tx(bar(FB2_KVFULL), 2 * C::TILE_BYTES);
+          for (int hh = 0; hh < C::HALVES; ++hh) {
+            tma_load_3d(sbase + C::OFF_K + hh * C::HALF_BYTES, &tm_k, bar(FB2_KVFULL), hh * 64,
+                        it.k0, it.bh_kv);
+            tma_load_3d(sbase + C::OFF_V + hh * C::HALF_BYTES, &tm_v, bar(FB2_KVFULL), hh * 64,
+                        it.k0, it.bh_kv);
+          }
         }
         __syncwarp();
-        issued_q[st] += 1;
-        // dO into its single stage once dV of the previous tile has read it
-        if (it > 0) ok = mbar_wait_warp(bar(FB2_DOEMPTY), (it - 1) & 1, abort_flag, 602);
-        if (!ok) break;
-        if (elect_one()) {
-          mbar_arrive_expect_tx(bar(FB2_DOFULL), C::TILE_BYTES);
-          for (int hh = 0; hh < C::HALVES; ++hh)
-            tma_load_3d(sbase + C::OFF_DO + hh * C::HALF_BYTES, &tm_do, bar(FB2_DOFULL),
-                        hh * 64, qi * 128, bh_q);
+        ++kv_loads;
+        for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
+          const int st = g & 1, u = g >> 1;
+          const int qi = it.qt_first + t % it.qt_per_head;
+          const int bh_q = it.b * p.Hq + it.hk * G + t / it.qt_per_head;
+          // Q (+ -LSE*log2e, -D) into stage st
+          if (u > 0) ok = mbar_wait_warp(bar(FB2_QEMPTY + st), (u - 1) & 1, abort_flag, 603);
+          if (!ok) break;
+          if (elect_one()) {
+            const uint32_t sq = sbase + C::OFF_Q + st * C::TILE_BYTES;
+            mbar_arrive_expect_tx(bar(FB2_QFULL + st), C::TILE_BYTES + 1024);
+            for (int hh = 0; hh < C::HALVES; ++hh)
+              tma_load_3d(sq + hh * C::HALF_BYTES, &tm_q, bar(FB2_QFULL + st), hh * 64,
+                          qi * 128, bh_q);
+            const size_t ws_off = (size_t)bh_q * p.Sq_pad + (size_t)qi * 128;
+            bulk_load(sbase + C::OFF_LSE + st * 512, p.ws_lse2 + ws_off, 512,
+                      bar(FB2_QFULL + st));
+            bulk_load(sbase + C::OFF_DELTA + st * 512, p.ws_delta + ws_off, 512,
+                      bar(FB2_QFULL + st));
+          }
+          __syncwarp();
+          issued_q[st] += 1;
+          // dO into its single stage once dV of the previous tile has read it
+          if (g > 0) ok = mbar_wait_warp(bar(FB2_DOEMPTY), (g - 1) & 1, abort_flag, 604);
+          if (!ok) break;
+          if (elect_one()) {
+            mbar_arrive_expect_tx(bar(FB2_DOFULL), C::TILE_BYTES);
+            for (int hh = 0; hh < C::HALVES; ++hh)
+              tma_load_3d(sbase + C::OFF_DO + hh * C::HALF_BYTES, &tm_do, bar(FB2_DOFULL),
+                          hh * 64, qi * 128, bh_q);
+          }
+          __syncwarp();
+          issued_do += 1;
         }
-        __syncwarp();
-        issued_do += 1;
       }
       if (!ok) {  // let the copies in flight land before the CTA exits
-        mbar_wait_noabort(bar(FB2_KV), 0, 603);
+        if (kv_loads) mbar_wait_noabort(bar(FB2_KVFULL), (kv_loads - 1) & 1, 605);
         for (int s = 0; s < 2; ++s)
-          if (issued_q[s]) mbar_wait_noabort(bar(FB2_QFULL + s), (issued_q[s] - 1) & 1, 603);
-        if (issued_do) mbar_wait_noabort(bar(FB2_DOFULL), (issued_do - 1) & 1, 603);
+          if (issued_q[s]) mbar_wait_noabort(bar(FB2_QFULL + s), (issued_q[s] - 1) & 1, 605);
+        if (issued_do) mbar_wait_noabort(bar(FB2_DOFULL), (issued_do - 1) & 1, 605);
       }
-    } else if (warp == kFusedMmaWarp && n_tiles > 0) {
+    } else if (warp == kFusedMmaWarp) {
       // ---------------- MMA issuer (whole warp, one elected lane issues) --------
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);
@@ -287,55 +348,74 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         __syncwarp();
       };
-      bool ok = mbar_wait_warp(bar(FB2_KV), 0, abort_flag, 611);
-      if (ok) ok = mbar_wait_warp(bar(FB2_QFULL + 0), 0, abort_flag, 612);
-      if (ok) {
-        tc_fence_after();
-        issue_t(tmem + C::TM_ST, d_k, d_q0, FB2_SFULL);
-      }
-      if (ok) ok = mbar_wait_warp(bar(FB2_DOFULL), 0, abort_flag, 613);
-      if (ok) {
-        tc_fence_after();
-        issue_t(tmem + C::TM_DPT, d_v, d_do, FB2_DPFULL);
-      }
-      if (ok) ok = mbar_wait_warp(bar(FB2_PFULL), 0, abort_flag, 614);
-      if (ok) {
-        tc_fence_after();
-        issue_acc(tmem + C::TM_DV, tmem + C::TM_ST, m_do, false, FB2_DOEMPTY);
-      }
-      for (int it = 0; it < n_tiles && ok; ++it) {
-        const int st = it & 1;
-        const bool more = it + 1 < n_tiles;
-        if (more) {
-          ok = mbar_wait_warp(bar(FB2_QFULL + (st ^ 1)), ((it + 1) >> 1) & 1, abort_flag, 615);
-          if (!ok) break;
-          tc_fence_after();
-          issue_t(tmem + C::TM_ST, d_k, desc_adv(d_q0, (st ^ 1) * C::TILE_BYTES), FB2_SFULL);
-        }
-        ok = mbar_wait_warp(bar(FB2_DSFULL), it & 1, abort_flag, 616);
+      auto qdesc = [&](int g) { return desc_adv(d_q0, (g & 1) * C::TILE_BYTES); };
+      bool ok = true;
+      int kv_items = 0, g0 = 0;
+      for (int k = 0; ok; ++k) {
+        int w;
+        ok = take_item(k, w);
+        if (!ok || w < 0) break;
+        const FusedItem item = fused_item(p, w);
+        const int n = item.n_tiles;
+        if (n == 0) continue;
+        ok = mbar_wait_warp(bar(FB2_KVFULL), kv_items & 1, abort_flag, 611);
+        if (ok) ok = mbar_wait_warp(bar(FB2_QFULL + (g0 & 1)), (g0 >> 1) & 1, abort_flag, 612);
         if (!ok) break;
         tc_fence_after();
-        issue_acc(tmem + C::TM_DK, tmem + C::TM_DPT, desc_adv(m_q0, st * C::TILE_BYTES), it > 0,
-                  FB2_QEMPTY + st);
-        issue_dq();
-        if (more) {
-          ok = mbar_wait_warp(bar(FB2_DQEMPTY), it & 1, abort_flag, 617);
-          if (ok) ok = mbar_wait_warp(bar(FB2_DOFULL), (it + 1) & 1, abort_flag, 618);
+        issue_t(tmem + C::TM_ST, d_k, qdesc(g0), FB2_SFULL);
+        // dP^T_0 reuses the dQ columns of the previous item's last tile
+        if (g0 > 0) ok = mbar_wait_warp(bar(FB2_DQEMPTY), (g0 - 1) & 1, abort_flag, 613);
+        if (ok) ok = mbar_wait_warp(bar(FB2_DOFULL), g0 & 1, abort_flag, 614);
+        if (!ok) break;
+        tc_fence_after();
+        issue_t(tmem + C::TM_DPT, d_v, d_do, FB2_DPFULL);
+        // the previous item's dK/dV have left TMEM
+        if (kv_items > 0)
+          ok = mbar_wait_warp(bar(FB2_ACCFREE), (kv_items - 1) & 1, abort_flag, 615);
+        if (ok) ok = mbar_wait_warp(bar(FB2_PFULL), g0 & 1, abort_flag, 616);
+        if (!ok) break;
+        tc_fence_after();
+        issue_acc(tmem + C::TM_DV, tmem + C::TM_ST, m_do, false, FB2_DOEMPTY);
+        for (int it = 0; it < n && ok; ++it) {
+          const int g = g0 + it;
+          const bool more = it + 1 < n;
+          if (more) {
+            ok = mbar_wait_warp(bar(FB2_QFULL + ((g + 1) & 1)), ((g + 1) >> 1) & 1, abort_flag,
+                                617);
+            if (!ok) break;
+            tc_fence_after();
+            issue_t(tmem + C::TM_ST, d_k, qdesc(g + 1), FB2_SFULL);
+          }
+          ok = mbar_wait_warp(bar(FB2_DSFULL), g & 1, abort_flag, 618);
           if (!ok) break;
           tc_fence_after();
-          issue_t(tmem + C::TM_DPT, d_v, d_do, FB2_DPFULL);
-          ok = mbar_wait_warp(bar(FB2_PFULL), (it + 1) & 1, abort_flag, 619);
-          if (!ok) break;
-          tc_fence_after();
-          issue_acc(tmem + C::TM_DV, tmem + C::TM_ST, m_do, true, FB2_DOEMPTY);
+          issue_acc(tmem + C::TM_DK, tmem + C::TM_DPT,
+                    desc_adv(m_q0, (g & 1) * C::TILE_BYTES), it > 0, FB2_QEMPTY + (g & 1));
+          issue_dq();
+          if (!more) {
+            if (elect_one()) {
+              tc_commit(bar(FB2_KVEMPTY));  // S^T, dP^T, dQ of this item are all issued
+              tc_commit(bar(FB2_ACC));
+            }
+            __syncwarp();
+          } else {
+            ok = mbar_wait_warp(bar(FB2_DQEMPTY), g & 1, abort_flag, 619);
+            if (ok) ok = mbar_wait_warp(bar(FB2_DOFULL), (g + 1) & 1, abort_flag, 620);
+            if (!ok) break;
+            tc_fence_after();
+            issue_t(tmem + C::TM_DPT, d_v, d_do, FB2_DPFULL);
+            ok = mbar_wait_warp(bar(FB2_PFULL), (g + 1) & 1, abort_flag, 621);
+            if (!ok) break;
+            tc_fence_after();
+            issue_acc(tmem + C::TM_DV, tmem + C::TM_ST, m_do, true, FB2_DOEMPTY);
+          }
         }
+        ++kv_items;
+        g0 += n;
       }
-      if (elect_one()) {
-        tc_commit(bar(FB2_ACC));
-        tc_commit(bar(FB2_DRAIN));
-      }
+      if (elect_one()) tc_commit(bar(FB2_DRAIN));
       __syncwarp();
-      mbar_wait_noabort(bar(FB2_DRAIN), 0, 620);
+      mbar_wait_noabort(bar(FB2_DRAIN), 0, 622);
     }
   } else if (warp >= 4) {
     // ------------- elementwise: warpgroup e owns query columns [64e, 64e+64);
@@ -344,111 +424,124 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_base = uint32_t(wq * 32) << 16;
-    const int key = k0 + row;
     const float sl2 = p.scale_log2;
     const int col0 = ewg * 64;
     // dS^T row `row` in the MN-major SW128 tile read by the dQ MMA: half ewg,
     // 16-byte chunk c of the row at physical chunk c ^ (row & 7)
     const uint32_t ds_row = sbase + C::OFF_DS + ewg * C::HALF_BYTES + row * 128;
     bool ok = true;
-    for (int it = 0; it < n_tiles && ok; ++it) {
-      const int st = it & 1;
-      const int qi = qt_first + it % qt_per_head;
-      const float4* s_lse = reinterpret_cast<const float4*>(smem + C::OFF_LSE + st * 512);
-      const float4* s_delta = reinterpret_cast<const float4*>(smem + C::OFF_DELTA + st * 512);
-      const bool diag = p.causal && qi * 128 < k0 + 127;
-      const int qlim = key - qi * 128;  // query columns with index < qlim are hidden (k > q)
-      ok = mbar_wait(bar(FB2_SFULL), it & 1, abort_flag, 621);
-      if (ok) ok = mbar_wait(bar(FB2_QFULL + st), (it >> 1) & 1, abort_flag, 622);
-      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
-      if (!ok) break;
-      tc_fence_after();
-      // Phase 1: P^T = 2^(s*scale*log2e - lse), 16 queries per step, packed to
-      // bf16 over columns already read; fp32 P kept for phase 2.  The next
-      // step's TMEM load is in flight while a step computes (the packed
-      // store of step s, columns [8s, 8s+8), never overlaps the load of
-      // step s+1, columns [16s+16, 16s+32)).
-      float pf[64];
-      uint32_t sr[2][16];
-      auto p_step = [&](auto mask_tag, int sub) {
-        constexpr bool kMask = decltype(mask_tag)::value;
-        const int c0 = col0 + sub * 16;
-        tmem_wait_ld();
-        if (sub < 3) tmem_ld16(tmem + lane_base + C::TM_ST + c0 + 16, sr[(sub + 1) & 1]);
-        const uint32_t(&cur)[16] = sr[sub & 1];
-        uint32_t pk[8];
+    int kv_items = 0, g0 = 0;
+    for (int k = 0; ok; ++k) {
+      int w;
+      ok = take_item(k, w);
+      if (!ok || w < 0) break;
+      const FusedItem item = fused_item(p, w);
+      const int key = item.k0 + row;
+      const bool valid = key < p.Sk;
+      __nv_bfloat16* out_row =
+          (ewg == 0 ? p.dv : p.dk) + ((size_t)item.bh_kv * p.Sk + (valid ? key : 0)) * D;
+      if (item.n_tiles == 0) {  // keys no query sees: zero gradients
+        if (valid) {
+          uint4* a4 = reinterpret_cast<uint4*>(out_row);
+          for (int v4 = 0; v4 < D / 8; ++v4) a4[v4] = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
+      for (int it = 0; it < item.n_tiles && ok; ++it) {
+        const int g = g0 + it;
+        const int st = g & 1;
+        const int qi = item.qt_first + it % item.qt_per_head;
+        const float4* s_lse = reinterpret_cast<const float4*>(smem + C::OFF_LSE + st * 512);
+        const float4* s_delta = reinterpret_cast<const float4*>(smem + C::OFF_DELTA + st * 512);
+        const bool diag = p.causal && qi * 128 < item.k0 + 127;
+        const int qlim = key - qi * 128;  // query columns with index < qlim are hidden (k > q)
+        ok = mbar_wait(bar(FB2_SFULL), g & 1, abort_flag, 631);
+        if (ok) ok = mbar_wait(bar(FB2_QFULL + st), (g >> 1) & 1, abort_flag, 632);
+        ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+        if (!ok) break;
+        tc_fence_after();
+        // Phase 1: P^T = 2^(s*scale*log2e - lse), 16 queries per step, packed to
+        // bf16 over columns already read; fp32 P kept for phase 2.  The next
+        // step's TMEM load is in flight while a step computes (the packed
+        // store of step s, columns [8s, 8s+8), never overlaps the load of
+        // step s+1, columns [16s+16, 16s+32)).
+        float pf[64];
+        uint32_t sr[2][16];
+        auto p_step = [&](auto mask_tag, int sub) {
+          constexpr bool kMask = decltype(mask_tag)::value;
+          const int c0 = col0 + sub * 16;
+          tmem_wait_ld();
+          if (sub < 3) tmem_ld16(tmem + lane_base + C::TM_ST + c0 + 16, sr[(sub + 1) & 1]);
+          const uint32_t(&cur)[16] = sr[sub & 1];
+          uint32_t pk[8];
 #pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const float4 l4 = s_lse[c0 / 4 + v4];  // -lse2
-          const float nl[4] = {l4.x, l4.y, l4.z, l4.w};
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const float4 l4 = s_lse[c0 / 4 + v4];  // -lse2
+            const float nl[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = v4 * 4 + e;
-            float pe = ex2_approx(fmaf(__uint_as_float(cur[i]), sl2, nl[e]));
-            if (kMask && c0 + i < qlim) pe = 0.0f;
-            pf[sub * 16 + i] = pe;
+            for (int e = 0; e < 4; ++e) {
+              const int i = v4 * 4 + e;
+              float pe = ex2_approx(fmaf(__uint_as_float(cur[i]), sl2, nl[e]));
+              if (kMask && c0 + i < qlim) pe = 0.0f;
+              pf[sub * 16 + i] = pe;
+            }
+            pk[2 * v4] = pack_bf16x2(pf[sub * 16 + 4 * v4], pf[sub * 16 + 4 * v4 + 1]);
+            pk[2 * v4 + 1] = pack_bf16x2(pf[sub * 16 + 4 * v4 + 2], pf[sub * 16 + 4 * v4 + 3]);
           }
-          pk[2 * v4] = pack_bf16x2(pf[sub * 16 + 4 * v4], pf[sub * 16 + 4 * v4 + 1]);
-          pk[2 * v4 + 1] = pack_bf16x2(pf[sub * 16 + 4 * v4 + 2], pf[sub * 16 + 4 * v4 + 3]);
+          tmem_st8(tmem + lane_base + C::TM_ST + col0 + sub * 8, pk);
+        };
+        tmem_ld16(tmem + lane_base + C::TM_ST + col0, sr[0]);
+        if (diag) {
+#pragma unroll
+          for (int sub = 0; sub < 4; ++sub) p_step(std::true_type{}, sub);
+        } else {
+#pragma unroll
+          for (int sub = 0; sub < 4; ++sub) p_step(std::false_type{}, sub);
         }
-        tmem_st8(tmem + lane_base + C::TM_ST + col0 + sub * 8, pk);
-      };
-      tmem_ld16(tmem + lane_base + C::TM_ST + col0, sr[0]);
-      if (diag) {
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(FB2_PFULL));
+        // Phase 2: dS^T = P^T (dP^T - D): bf16 packed over dP^T (A of dK) and
+        // into the shared dS tile (A of dQ).
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(FB2_DPFULL), g & 1, abort_flag, 633));
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t dr[2][16];
+        tmem_ld16(tmem + lane_base + C::TM_DPT + col0, dr[0]);
 #pragma unroll
-        for (int sub = 0; sub < 4; ++sub) p_step(std::true_type{}, sub);
-      } else {
+        for (int sub = 0; sub < 4; ++sub) {
+          const int c0 = col0 + sub * 16;
+          tmem_wait_ld();
+          if (sub < 3) tmem_ld16(tmem + lane_base + C::TM_DPT + c0 + 16, dr[(sub + 1) & 1]);
+          const uint32_t(&cur)[16] = dr[sub & 1];
+          uint32_t dk[8];
 #pragma unroll
-        for (int sub = 0; sub < 4; ++sub) p_step(std::false_type{}, sub);
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const float4 d4 = s_delta[c0 / 4 + v4];  // -D
+            const float nd[4] = {d4.x, d4.y, d4.z, d4.w};
+            float dsv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              dsv[e] = pf[sub * 16 + v4 * 4 + e] * (__uint_as_float(cur[v4 * 4 + e]) + nd[e]);
+            dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
+            dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
+          }
+          tmem_st8(tmem + lane_base + C::TM_DPT + col0 + sub * 8, dk);
+          const uint32_t ch = uint32_t(2 * sub);
+          st_shared_v4(ds_row + ((ch ^ uint32_t(row & 7)) << 4), dk[0], dk[1], dk[2], dk[3]);
+          st_shared_v4(ds_row + (((ch + 1) ^ uint32_t(row & 7)) << 4), dk[4], dk[5], dk[6],
+                       dk[7]);
+        }
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar(FB2_DSFULL));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(FB2_PFULL));
-      // Phase 2: dS^T = P^T (dP^T - D): bf16 packed over dP^T (A of dK) and
-      // into the shared dS tile (A of dQ).
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(FB2_DPFULL), it & 1, abort_flag, 623));
       if (!ok) break;
-      tc_fence_after();
-      uint32_t dr[2][16];
-      tmem_ld16(tmem + lane_base + C::TM_DPT + col0, dr[0]);
-#pragma unroll
-      for (int sub = 0; sub < 4; ++sub) {
-        const int c0 = col0 + sub * 16;
-        tmem_wait_ld();
-        if (sub < 3) tmem_ld16(tmem + lane_base + C::TM_DPT + c0 + 16, dr[(sub + 1) & 1]);
-        const uint32_t(&cur)[16] = dr[sub & 1];
-        uint32_t dk[8];
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const float4 d4 = s_delta[c0 / 4 + v4];  // -D
-          const float nd[4] = {d4.x, d4.y, d4.z, d4.w};
-          float dsv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            dsv[e] = pf[sub * 16 + v4 * 4 + e] * (__uint_as_float(cur[v4 * 4 + e]) + nd[e]);
-          dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
-          dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
-        }
-        tmem_st8(tmem + lane_base + C::TM_DPT + col0 + sub * 8, dk);
-        const uint32_t ch = uint32_t(2 * sub);
-        st_shared_v4(ds_row + ((ch ^ uint32_t(row & 7)) << 4), dk[0], dk[1], dk[2], dk[3]);
-        st_shared_v4(ds_row + (((ch + 1) ^ uint32_t(row & 7)) << 4), dk[4], dk[5], dk[6], dk[7]);
-      }
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(bar(FB2_DSFULL));
-    }
-    // ---- epilogue: warpgroup 0 writes dV, 1 writes dK (= acc * scale)
-    const bool valid = key < p.Sk;
-    __nv_bfloat16* out_row =
-        (ewg == 0 ? p.dv : p.dk) + ((size_t)bh_kv * p.Sk + (valid ? key : 0)) * D;
-    if (n_tiles == 0) {
-      if (valid) {
-        uint4* a4 = reinterpret_cast<uint4*>(out_row);
-        for (int v4 = 0; v4 < D / 8; ++v4) a4[v4] = make_uint4(0, 0, 0, 0);
-      }
-    } else if (__all_sync(0xffffffffu, ok && mbar_wait(bar(FB2_ACC), 0, abort_flag, 624))) {
+      // ---- epilogue: warpgroup 0 writes dV, 1 writes dK (= acc * scale); the
+      // accumulators are released once read, while the stores drain
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(FB2_ACC), kv_items & 1, abort_flag, 634));
+      if (!ok) break;
       tc_fence_after();
       const uint32_t acc_col = ewg == 0 ? C::TM_DV : C::TM_DK;
       const float mul = ewg == 0 ? 1.0f : p.scale;
@@ -457,8 +550,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + acc_col + c * 32, r);
         tmem_wait_ld();
+        if (c == D / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(bar(FB2_ACCFREE));
+        }
         if (valid) store_row_chunk_bf16(out_row + c * 32, r, mul);
       }
+      ++kv_items;
+      g0 += item.n_tiles;
     }
   } else {
     // ------------- dQ reduction: thread = query row of the tile
@@ -467,40 +566,46 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const uint32_t lane_base = uint32_t(warp * 32) << 16;
     const uint32_t stg_row = sbase + C::OFF_STG + row * 128;
     bool ok = true;
-    for (int it = 0; it < n_tiles && ok; ++it) {
-      const int g = it / qt_per_head;
-      const int qi = qt_first + it % qt_per_head;
-      const int bh_q = b * p.Hq + hk * G + g;
-      const int grow0 = bh_q * p.Sq_pad + qi * 128;  // first accumulator row of the tile
-      // the four warps agree before any of them reaches the named barriers below
-      ok = named_bar_and(1, 128, mbar_wait(bar(FB2_DQFULL), it & 1, abort_flag, 631));
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t acc[D];
+    int g = 0;
+    for (int k = 0; ok; ++k) {
+      int w;
+      ok = named_bar_and(1, 128, take_item(k, w));
+      if (!ok || w < 0) break;
+      const FusedItem item = fused_item(p, w);
+      for (int t = 0; t < item.n_tiles && ok; ++t, ++g) {
+        const int qi = item.qt_first + t % item.qt_per_head;
+        const int bh_q = item.b * p.Hq + item.hk * G + t / item.qt_per_head;
+        const int grow0 = bh_q * p.Sq_pad + qi * 128;  // first accumulator row of the tile
+        // the four warps agree before any of them reaches the named barriers below
+        ok = named_bar_and(1, 128, mbar_wait(bar(FB2_DQFULL), g & 1, abort_flag, 641));
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t acc[D];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c)
-        tmem_ld32(tmem + lane_base + C::TM_DPT + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar(FB2_DQEMPTY));
+        for (int c = 0; c < D / 32; ++c)
+          tmem_ld32(tmem + lane_base + C::TM_DPT + c * 32,
+                    *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar(FB2_DQEMPTY));
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        // chunk c of every tile uses buffer c & 1 (D / 32 chunks per tile is even)
-        const uint32_t buf = uint32_t(c & 1) * (C::STG_BYTES / 2);
-        // the reduction issued two chunks ago (same buffer) must have read it
-        if (threadIdx.x == 0) bulk_wait_group_read1();
-        named_bar_sync(1, 128);
+        for (int c = 0; c < D / 32; ++c) {
+          // chunk c of every tile uses buffer c & 1 (D / 32 chunks per tile is even)
+          const uint32_t buf = uint32_t(c & 1) * (C::STG_BYTES / 2);
+          // the reduction issued two chunks ago (same buffer) must have read it
+          if (threadIdx.x == 0) bulk_wait_group_read1();
+          named_bar_sync(1, 128);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          st_shared_v4(stg_row + buf + ((uint32_t(j) ^ uint32_t(row & 7)) << 4),
-                       acc[c * 32 + 4 * j], acc[c * 32 + 4 * j + 1], acc[c * 32 + 4 * j + 2],
-                       acc[c * 32 + 4 * j + 3]);
-        fence_proxy_async_smem();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == 0) {
-          tma_reduce_add_2d(&tm_dqacc, sbase + C::OFF_STG + buf, c * 32, grow0);
-          bulk_commit_group();
+          for (int j = 0; j < 8; ++j)
+            st_shared_v4(stg_row + buf + ((uint32_t(j) ^ uint32_t(row & 7)) << 4),
+                         acc[c * 32 + 4 * j], acc[c * 32 + 4 * j + 1], acc[c * 32 + 4 * j + 2],
+                         acc[c * 32 + 4 * j + 3]);
+          fence_proxy_async_smem();
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 0) {
+            tma_reduce_add_2d(&tm_dqacc, sbase + C::OFF_STG + buf, c * 32, grow0);
+            bulk_commit_group();
+          }
         }
       }
     }

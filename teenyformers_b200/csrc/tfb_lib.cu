@@ -256,14 +256,15 @@ int bwd_bf16_impl(const void* q, const void* k, const void* v, const void* o, co
   float* ws_delta = ws_lse2 + bhq * sq_pad;
   const long long rows = bhq * sq_pad;
   float* dq_acc = fused ? ws_delta + bhq * sq_pad : nullptr;  // 256-byte aligned
+  int* counter = fused ? reinterpret_cast<int*>(dq_acc + bhq * sq_pad * 128) : nullptr;
   if (head_dim == 128)
     fa_bwd_prep_kernel<128><<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(d_o), lse,
-        ws_lse2, ws_delta, dq_acc, n_ctx_q, sq_pad, rows);
+        ws_lse2, ws_delta, dq_acc, counter, n_ctx_q, sq_pad, rows);
   else
     fa_bwd_prep_kernel<64><<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(d_o), lse,
-        ws_lse2, ws_delta, dq_acc, n_ctx_q, sq_pad, rows);
+        ws_lse2, ws_delta, dq_acc, counter, n_ctx_q, sq_pad, rows);
   if (int e = launch_status()) return e;
 
   CUtensorMap tq, tdo, tk, tv;
@@ -290,6 +291,8 @@ int bwd_bf16_impl(const void* q, const void* k, const void* v, const void* o, co
   prm.scale = softmax_scale;
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
+  prm.work_counter = counter;
+  prm.n_items = (int)(bhkv * prm.n_kt);
   const dim3 grid_kv((unsigned)(bhkv * prm.n_kt));
   if (fused) {
     if (!fits_i32(rows)) return TF_ERR_TOO_LARGE;  // accumulator row index is int
@@ -299,13 +302,15 @@ int bwd_bf16_impl(const void* q, const void* k, const void* v, const void* o, co
     const long long groups = out_rows * (head_dim / 8);
     const unsigned cgrid = (unsigned)std::min<long long>((groups + 255) / 256, 148LL * 16);
     if (head_dim == 128) {
-      fa_bwd_fused_sm100_kernel<128><<<grid_kv, kFusedThreads, BwdFusedCfg<128>::SMEM_BYTES,
-                                       st>>>(tq, tdo, tk, tv, tacc, prm);
+      fa_bwd_fused_sm100_kernel<128><<<persistent_grid(prm.n_items), kFusedThreads,
+                                       BwdFusedCfg<128>::SMEM_BYTES, st>>>(tq, tdo, tk, tv, tacc,
+                                                                           prm);
       fa_bwd_dq_convert_kernel<128><<<cgrid, 256, 0, st>>>(
           dq_acc, prm.dq, n_ctx_q, sq_pad, out_rows, softmax_scale);
     } else {
-      fa_bwd_fused_sm100_kernel<64><<<grid_kv, kFusedThreads, BwdFusedCfg<64>::SMEM_BYTES,
-                                      st>>>(tq, tdo, tk, tv, tacc, prm);
+      fa_bwd_fused_sm100_kernel<64><<<persistent_grid(prm.n_items), kFusedThreads,
+                                      BwdFusedCfg<64>::SMEM_BYTES, st>>>(tq, tdo, tk, tv, tacc,
+                                                                         prm);
       fa_bwd_dq_convert_kernel<64><<<cgrid, 256, 0, st>>>(
           dq_acc, prm.dq, n_ctx_q, sq_pad, out_rows, softmax_scale);
     }

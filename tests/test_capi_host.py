@@ -67,9 +67,10 @@ def test_empty_problems_are_noops(native_lib):
 
 def test_bwd_workspace_size(native_lib):
     # -LSE*log2e and -D rows plus the fp32 dQ accumulator (128 columns), all
-    # over B*Hq rows padded to a multiple of 128 queries
+    # over B*Hq rows padded to a multiple of 128 queries, and a 256-byte
+    # work-item counter
     n = _capi.raw("tf_b200_flash_attn2_bwd_workspace_size", 2, 3, 130)
-    assert n == (2 + 128) * 2 * 3 * 256 * 4
+    assert n == (2 + 128) * 2 * 3 * 256 * 4 + 256
     assert _capi.raw("tf_b200_flash_attn2_bwd_workspace_size", 0, 3, 130) == 0
 
 
