@@ -9,8 +9,8 @@
 //
 // Layout in HBM: Q, O [B*Hq, Sq, D]; K, V [B*Hkv, Sk, D]; LSE [B*Hq, Sq] fp32.
 //
-// One CTA owns two 128-row query tiles of one head (rows q0..q0+255) and
-// walks 128-row key/value tiles:
+// Persistent (one CTA per SM); each work item is two 128-row query tiles of
+// one head (rows q0..q0+255), walked over 128-row key/value tiles:
 //   warp 9     TMA producer: Q once, then K_j / V_j into 2-stage rings
 //   warp 8     MMA issuer (one thread): S_t = Q_t K_j^T  (SS, M=128 N=128),
 //              O_t += P_t V_j (A = P from TMEM, B = V from SMEM, N = D)
@@ -74,7 +74,9 @@ enum FwdBar {
   FB_ODONE = 13,  // 2
   FB_DRAIN = 15,
   FB_PFULL1 = 16,  // 2: keys 64..127 of P_t ready
-  FB_COUNT = 18
+  FB_QEMPTY = 18,  // every S MMA of the item is done: Q may be replaced
+  FB_OFREE = 19,   // 2: the epilogue has read O_t out of TMEM
+  FB_COUNT = 21
 };
 
 // Waits without looking at the abort flag (used to drain in-flight async
@@ -83,6 +85,44 @@ __device__ __forceinline__ void mbar_drain_wait(uint32_t bar, uint32_t parity, i
   (void)mbar_wait(bar, parity, nullptr, site);
 }
 
+// Work item w = query-tile pair of one head: head-major (the CTAs running at
+// any time share a few heads' K/V in L2), heavy (late) pairs first within a
+// head when causal.  Each role derives the same values from w.
+struct FwdItem {
+  int bh, bh_kv, q0, nkv0, nkv1, n_iter;
+};
+__device__ __forceinline__ FwdItem fwd_item(const FwdParams& p, int w) {
+  FwdItem it;
+  it.bh = w / p.n_pairs;
+  int pair = w % p.n_pairs;
+  if (p.causal) pair = p.n_pairs - 1 - pair;
+  const int b = it.bh / p.Hq, h = it.bh % p.Hq;
+  it.bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
+  it.q0 = pair * 256;
+  const int n_kv_all = (p.Sk + 127) / 128;
+  auto tile_kv = [&](int t) {  // key tiles query tile t needs (0 if it is past Sq)
+    const int qs = it.q0 + 128 * t;
+    if (qs >= p.Sq) return 0;
+    if (!p.causal) return n_kv_all;
+    return min(n_kv_all, (min(p.Sq, qs + 128) - 1) / 128 + 1);
+  };
+  it.nkv0 = tile_kv(0);
+  it.nkv1 = tile_kv(1);
+  it.n_iter = max(it.nkv0, it.nkv1);
+  return it;
+}
+
+// Item of round k for this CTA: rounds alternate direction (boustrophedon), so
+// heavy and light items spread over the CTAs; only the last round is partial.
+__device__ __forceinline__ int fwd_sched(int k) {
+  const int G = gridDim.x, c = blockIdx.x;
+  return k * G + ((k & 1) ? G - 1 - c : c);
+}
+
+// Persistent: one CTA per SM walks work items (fwd_sched).  Per-step barriers
+// (S/P per tile, K/V ring) run on counts that continue across items; per item,
+// the next item's Q load starts once the last S MMA of the current item has
+// run, and its first O_t = P_t V MMA waits until the epilogue has read O_t.
 template <int D>
 __global__ void __launch_bounds__(320, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -97,31 +137,13 @@ __global__ void __launch_bounds__(320, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + FB_COUNT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto bar = [&](int i) { return smem_u32(bars + i); };
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // ---- work decode: head-major, so the CTAs resident at any time share a
-  // few heads' K/V in L2; within a head, heavy (late) pairs first for causal.
-  const int bh = blockIdx.x / p.n_pairs;
-  int pair = blockIdx.x % p.n_pairs;
-  if (p.causal) pair = p.n_pairs - 1 - pair;
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
-  const int q0 = pair * 256;
-  const int n_kv_all = (p.Sk + 127) / 128;
-  auto tile_kv = [&](int t) {  // key tiles query tile t needs (0 if it is past Sq)
-    const int qs = q0 + 128 * t;
-    if (qs >= p.Sq) return 0;
-    if (!p.causal) return n_kv_all;
-    return min(n_kv_all, (min(p.Sq, qs + 128) - 1) / 128 + 1);
-  };
-  const int nkv0 = tile_kv(0), nkv1 = tile_kv(1);
-  auto nkv = [&](int t) { return t ? nkv1 : nkv0; };
-  const int n_iter = max(nkv0, nkv1);
+  const int n_items = p.BHq * p.n_pairs;
 
   // ---- setup ----
   if (threadIdx.x == 0) {
     mbar_init(bar(FB_QFULL), 1);
+    mbar_init(bar(FB_QEMPTY), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(FB_KFULL + s), 1);
       mbar_init(bar(FB_KEMPTY + s), 1);
@@ -131,6 +153,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(FB_PFULL + s), 128);
       mbar_init(bar(FB_PFULL1 + s), 128);
       mbar_init(bar(FB_ODONE + s), 1);
+      mbar_init(bar(FB_OFREE + s), 128);
     }
     mbar_init(bar(FB_DRAIN), 1);
     *abort_flag = 0;
@@ -152,46 +175,55 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 9) {
     // =================== TMA producer (whole warp, one elected lane issues) =====
-    int issued_k0 = 0, issued_k1 = 0, issued_v0 = 0, issued_v1 = 0;
+    int issued_q = 0, issued_k[2] = {0, 0}, issued_v[2] = {0, 0}, gj = 0;
     bool ok = true;
-    if (elect_one()) {
-      mbar_arrive_expect_tx(bar(FB_QFULL), 2 * C::TILE_BYTES);
-      for (int t = 0; t < 2; ++t)
-        for (int hh = 0; hh < C::HALVES; ++hh)
-          tma_load_3d(sbase + C::OFF_Q + t * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_q,
-                      bar(FB_QFULL), hh * 64, q0 + 128 * t, bh);
-    }
-    __syncwarp();
-    for (int j = 0; j < n_iter && ok; ++j) {
-      const int s = j & 1, u = j >> 1;
-      if (u > 0) ok = mbar_wait_warp(bar(FB_KEMPTY + s), (u - 1) & 1, abort_flag, 101);
+    for (int k = 0; ok; ++k) {
+      const int w = fwd_sched(k);
+      if (w >= n_items) break;
+      const FwdItem it = fwd_item(p, w);
+      if (it.n_iter == 0) continue;
+      if (issued_q > 0) ok = mbar_wait_warp(bar(FB_QEMPTY), (issued_q - 1) & 1, abort_flag, 104);
       if (!ok) break;
       if (elect_one()) {
-        mbar_arrive_expect_tx(bar(FB_KFULL + s), C::TILE_BYTES);
-        for (int hh = 0; hh < C::HALVES; ++hh)
-          tma_load_3d(sbase + C::OFF_K + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_k,
-                      bar(FB_KFULL + s), hh * 64, j * 128, bh_kv);
+        mbar_arrive_expect_tx(bar(FB_QFULL), 2 * C::TILE_BYTES);
+        for (int t = 0; t < 2; ++t)
+          for (int hh = 0; hh < C::HALVES; ++hh)
+            tma_load_3d(sbase + C::OFF_Q + t * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_q,
+                        bar(FB_QFULL), hh * 64, it.q0 + 128 * t, it.bh);
       }
       __syncwarp();
-      (s ? issued_k1 : issued_k0) += 1;
-      if (u > 0) ok = mbar_wait_warp(bar(FB_VEMPTY + s), (u - 1) & 1, abort_flag, 102);
-      if (!ok) break;
-      if (elect_one()) {
-        mbar_arrive_expect_tx(bar(FB_VFULL + s), C::TILE_BYTES);
-        for (int hh = 0; hh < C::HALVES; ++hh)
-          tma_load_3d(sbase + C::OFF_V + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v,
-                      bar(FB_VFULL + s), hh * 64, j * 128, bh_kv);
+      ++issued_q;
+      for (int j = 0; j < it.n_iter && ok; ++j, ++gj) {
+        const int s = gj & 1, u = gj >> 1;
+        if (u > 0) ok = mbar_wait_warp(bar(FB_KEMPTY + s), (u - 1) & 1, abort_flag, 101);
+        if (!ok) break;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(bar(FB_KFULL + s), C::TILE_BYTES);
+          for (int hh = 0; hh < C::HALVES; ++hh)
+            tma_load_3d(sbase + C::OFF_K + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_k,
+                        bar(FB_KFULL + s), hh * 64, j * 128, it.bh_kv);
+        }
+        __syncwarp();
+        issued_k[s] += 1;
+        if (u > 0) ok = mbar_wait_warp(bar(FB_VEMPTY + s), (u - 1) & 1, abort_flag, 102);
+        if (!ok) break;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(bar(FB_VFULL + s), C::TILE_BYTES);
+          for (int hh = 0; hh < C::HALVES; ++hh)
+            tma_load_3d(sbase + C::OFF_V + s * C::TILE_BYTES + hh * C::HALF_BYTES, &tm_v,
+                        bar(FB_VFULL + s), hh * 64, j * 128, it.bh_kv);
+        }
+        __syncwarp();
+        issued_v[s] += 1;
       }
-      __syncwarp();
-      (s ? issued_v1 : issued_v0) += 1;
     }
     if (!ok) {
       // Abort: let every issued copy land before the CTA's smem goes away.
-      mbar_drain_wait(bar(FB_QFULL), 0, 103);
-      if (issued_k0) mbar_drain_wait(bar(FB_KFULL + 0), (issued_k0 - 1) & 1, 103);
-      if (issued_k1) mbar_drain_wait(bar(FB_KFULL + 1), (issued_k1 - 1) & 1, 103);
-      if (issued_v0) mbar_drain_wait(bar(FB_VFULL + 0), (issued_v0 - 1) & 1, 103);
-      if (issued_v1) mbar_drain_wait(bar(FB_VFULL + 1), (issued_v1 - 1) & 1, 103);
+      if (issued_q) mbar_drain_wait(bar(FB_QFULL), (issued_q - 1) & 1, 103);
+      for (int s = 0; s < 2; ++s) {
+        if (issued_k[s]) mbar_drain_wait(bar(FB_KFULL + s), (issued_k[s] - 1) & 1, 103);
+        if (issued_v[s]) mbar_drain_wait(bar(FB_VFULL + s), (issued_v[s] - 1) & 1, 103);
+      }
     }
   } else if (warp == 8) {
     // =================== MMA issuer (whole warp, one elected lane issues) =======
@@ -237,53 +269,84 @@ __global__ void __launch_bounds__(320, 1)
       }
       __syncwarp();
     };
-    bool ok = mbar_wait_warp(bar(FB_QFULL), 0, abort_flag, 201);
-    if (ok && n_iter > 0) ok = mbar_wait_warp(bar(FB_KFULL + 0), 0, abort_flag, 202);
-    if (ok && n_iter > 0) {
+    auto commit = [&](int b0) {
+      if (elect_one()) tc_commit(bar(b0));
+      __syncwarp();
+    };
+    bool ok = true;
+    // n_q: items with work so far (QFULL/QEMPTY phases); gj: K/V steps so far;
+    // st_[t]: steps of query tile t so far (S/P phases); no_[t]: items in which
+    // tile t had work (ODONE/OFREE phases)
+    int n_q = 0, gj = 0, st_[2] = {0, 0}, no_[2] = {0, 0};
+    for (int k = 0; ok; ++k) {
+      const int w = fwd_sched(k);
+      if (w >= n_items) break;
+      const FwdItem it = fwd_item(p, w);
+      if (it.n_iter == 0) continue;
+      auto nkv = [&](int t) { return t ? it.nkv1 : it.nkv0; };
+      ok = mbar_wait_warp(bar(FB_QFULL), n_q & 1, abort_flag, 201);
+      if (ok) ok = mbar_wait_warp(bar(FB_KFULL + (gj & 1)), (gj >> 1) & 1, abort_flag, 202);
+      if (!ok) break;
       tc_fence_after();
       for (int t = 0; t < 2; ++t)
-        if (nkv(t) > 0) issue_qk(t, 0);
-      if (elect_one()) tc_commit(bar(FB_KEMPTY + 0));
-      __syncwarp();
-    }
-    // Slot-release commits of the previous iteration are issued once the next
-    // batch of MMAs is queued.
-    int pend_v = -1, pend_k = -1;
-    for (int j = 0; j < n_iter && ok; ++j) {
-      const int s = j & 1;
-      const int sn = (j + 1) & 1;
-      bool v_ready = false, k_next_ready = false;
-      for (int t = 0; t < 2 && ok; ++t) {
-        if (j >= nkv(t)) continue;
-        if (!v_ready) {
-          ok = mbar_wait_warp(bar(FB_VFULL + s), (j >> 1) & 1, abort_flag, 203);
-          if (!ok) break;
-          v_ready = true;
-        }
-        ok = mbar_wait_warp(bar(FB_PFULL + t), j & 1, abort_flag, 204);  // keys 0..63 of P_t(j)
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv_half(t, s, 0, j > 0, pend_v >= 0 ? FB_VEMPTY + pend_v : -1,
-                      pend_k >= 0 ? FB_KEMPTY + pend_k : -1);
-        pend_v = pend_k = -1;
-        ok = mbar_wait_warp(bar(FB_PFULL1 + t), j & 1, abort_flag, 207);  // keys 64..127
-        if (!ok) break;
-        tc_fence_after();
-        const bool more = j + 1 < nkv(t);
-        issue_pv_half(t, s, 1, true, more ? -1 : FB_ODONE + t, -1);
-        if (more) {
-          if (!k_next_ready) {
-            ok = mbar_wait_warp(bar(FB_KFULL + sn), ((j + 1) >> 1) & 1, abort_flag, 205);
+        if (nkv(t) > 0) issue_qk(t, gj & 1);
+      if (it.n_iter == 1) commit(FB_QEMPTY);  // that was the item's last S MMA
+      commit(FB_KEMPTY + (gj & 1));
+      // Slot-release commits of a step are issued once the next batch of MMAs
+      // is queued.
+      int pend_v = -1, pend_k = -1;
+      for (int j = 0; j < it.n_iter && ok; ++j) {
+        const int s = (gj + j) & 1;
+        const int sn = (gj + j + 1) & 1;
+        bool v_ready = false, k_next_ready = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= nkv(t)) continue;
+          if (!v_ready) {
+            ok = mbar_wait_warp(bar(FB_VFULL + s), ((gj + j) >> 1) & 1, abort_flag, 203);
             if (!ok) break;
-            tc_fence_after();
-            k_next_ready = true;
+            v_ready = true;
           }
-          issue_qk(t, sn);
+          if (j == 0 && no_[t] > 0) {  // the previous item's epilogue has read O_t
+            ok = mbar_wait_warp(bar(FB_OFREE + t), (no_[t] - 1) & 1, abort_flag, 208);
+            if (!ok) break;
+          }
+          const uint32_t ph = uint32_t(st_[t] + j) & 1u;
+          ok = mbar_wait_warp(bar(FB_PFULL + t), ph, abort_flag, 204);  // keys 0..63 of P_t
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv_half(t, s, 0, j > 0, pend_v >= 0 ? FB_VEMPTY + pend_v : -1,
+                        pend_k >= 0 ? FB_KEMPTY + pend_k : -1);
+          pend_v = pend_k = -1;
+          ok = mbar_wait_warp(bar(FB_PFULL1 + t), ph, abort_flag, 207);  // keys 64..127
+          if (!ok) break;
+          tc_fence_after();
+          const bool more = j + 1 < nkv(t);
+          issue_pv_half(t, s, 1, true, more ? -1 : FB_ODONE + t, -1);
+          if (more) {
+            if (!k_next_ready) {
+              ok = mbar_wait_warp(bar(FB_KFULL + sn), ((gj + j + 1) >> 1) & 1, abort_flag, 205);
+              if (!ok) break;
+              tc_fence_after();
+              k_next_ready = true;
+            }
+            issue_qk(t, sn);
+          }
         }
+        if (!ok) break;
+        pend_v = s;
+        pend_k = (j + 1 < it.n_iter) ? sn : -1;
+        if (j + 2 == it.n_iter) commit(FB_QEMPTY);  // the item's last S MMAs are queued
       }
       if (!ok) break;
-      pend_v = s;
-      pend_k = (j + 1 < n_iter) ? sn : -1;
+      // release the item's last V slot before moving on
+      if (pend_v >= 0) commit(FB_VEMPTY + pend_v);
+      if (pend_k >= 0) commit(FB_KEMPTY + pend_k);
+      gj += it.n_iter;
+      ++n_q;
+      for (int t = 0; t < 2; ++t) {
+        st_[t] += nkv(t);
+        if (nkv(t) > 0) ++no_[t];
+      }
     }
     // Drain: every MMA issued above completes before TMEM is released.
     if (elect_one()) tc_commit(bar(FB_DRAIN));
@@ -297,118 +360,132 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_base = uint32_t(wq * 32) << 16;
     const uint32_t tS = tmem + lane_base + C::tm_s(t);
     const uint32_t tO = tmem + lane_base + C::tm_o(t);
-    const int qs = q0 + 128 * t;
-    const int q_idx = qs + row;
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < nkv(t); ++j) {
-      ok = mbar_wait(bar(FB_SFULL + t), j & 1, abort_flag, 300 + t);
-      ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+    int st_t = 0, no_t = 0;  // this tile's steps / items with work so far
+    for (int k = 0; ok; ++k) {
+      const int w = fwd_sched(k);
+      if (w >= n_items) break;
+      const FwdItem it = fwd_item(p, w);
+      const int nk = t ? it.nkv1 : it.nkv0;
+      if (nk == 0) continue;
+      const int qs = it.q0 + 128 * t;
+      const int q_idx = qs + row;
+      float m = -INFINITY, l = 0.0f;
+      for (int j = 0; j < nk; ++j) {
+        ok = mbar_wait(bar(FB_SFULL + t), uint32_t(st_t + j) & 1u, abort_flag, 300 + t);
+        ok = __all_sync(0xffffffffu, ok);  // keep .sync.aligned TMEM ops convergent
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sr[4][32];
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
+        tmem_wait_ld();
+        const int kbase = j * 128;
+        const bool need_mask = (p.causal && kbase + 127 > qs) || (kbase + 128 > p.Sk);
+        if (need_mask) {
+          int lim = p.Sk - 1 - kbase;  // keys with index > lim are hidden
+          if (p.causal) lim = min(lim, q_idx - kbase);
+  #pragma unroll
+          for (int c = 0; c < 4; ++c)
+  #pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
+        }
+        // row max: 3-input max, four independent chains
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  #pragma unroll
+        for (int c = 0; c < 4; ++c)
+  #pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], __uint_as_float(sr[c][i]),
+                                     __uint_as_float(sr[c][i + 1]));
+        const float rmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        const float m_new = fmaxf(m, rmax * sl2);
+        const bool resc = m_new > m + 8.0f;
+        const float m_use = resc ? m_new : m;
+        const float alpha = resc ? ex2_approx(m - m_use) : 1.0f;
+        const float base = (m_use == -INFINITY) ? 0.0f : m_use;
+        const uint64_t sl2x2 = f2_make(sl2, sl2);
+        const uint64_t nbx2 = f2_make(-base, -base);
+        uint64_t acc2[2] = {f2_make(0.0f, 0.0f), f2_make(0.0f, 0.0f)};
+        // P = 2^(s*scale*log2e - m) in bf16, written over the S columns already
+        // read, 32 keys per store; handed off per 64-key half.
+  #pragma unroll
+        for (int half = 0; half < 2; ++half) {
+  #pragma unroll
+          for (int c = 2 * half; c < 2 * half + 2; ++c) {
+            uint32_t pk[16];
+  #pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const uint64_t x2 = f2_fma(
+                  f2_make(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])), sl2x2,
+                  nbx2);
+              float x0, x1;
+              f2_split(x2, x0, x1);
+              const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+              acc2[i & 1] = f2_add(acc2[i & 1], f2_make(p0, p1));
+              pk[i] = pack_bf16x2(p0, p1);
+            }
+            tmem_st16(tS + c * 16, pk);
+          }
+          if (half == 0 && j > 0 && __any_sync(0xffffffffu, resc)) {
+            // PV(j-1) of this tile completed before S(j) was signalled.
+  #pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t orow[32];
+              tmem_ld32(tO + c * 32, orow);
+              tmem_wait_ld();
+  #pragma unroll
+              for (int i = 0; i < 32; ++i)
+                orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+              tmem_st32(tO + c * 32, orow);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar((half == 0 ? FB_PFULL : FB_PFULL1) + t));
+        }
+        float a0, a1, a2, a3;
+        f2_split(acc2[0], a0, a1);
+        f2_split(acc2[1], a2, a3);
+        l = l * alpha + ((a0 + a1) + (a2 + a3));
+        m = m_use;
+      }
+      if (!ok) break;
+      // ---- epilogue: O / l (bf16) and LSE; O_t is released to the next item's
+      // first P V MMA once read, while the stores drain
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(FB_ODONE + t), uint32_t(no_t) & 1u, abort_flag,
+                                             310 + t));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
-      tmem_wait_ld();
-      const int kbase = j * 128;
-      const bool need_mask = (p.causal && kbase + 127 > qs) || (kbase + 128 > p.Sk);
-      if (need_mask) {
-        int lim = p.Sk - 1 - kbase;  // keys with index > lim are hidden
-        if (p.causal) lim = min(lim, q_idx - kbase);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
-      }
-      // row max: 3-input max, four independent chains
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; i += 2)
-          mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], __uint_as_float(sr[c][i]),
-                                   __uint_as_float(sr[c][i + 1]));
-      const float rmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      const float m_new = fmaxf(m, rmax * sl2);
-      const bool resc = m_new > m + 8.0f;
-      const float m_use = resc ? m_new : m;
-      const float alpha = resc ? ex2_approx(m - m_use) : 1.0f;
-      const float base = (m_use == -INFINITY) ? 0.0f : m_use;
-      const uint64_t sl2x2 = f2_make(sl2, sl2);
-      const uint64_t nbx2 = f2_make(-base, -base);
-      uint64_t acc2[2] = {f2_make(0.0f, 0.0f), f2_make(0.0f, 0.0f)};
-      // P = 2^(s*scale*log2e - m) in bf16, written over the S columns already
-      // read, 32 keys per store; handed off per 64-key half.
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-#pragma unroll
-        for (int c = 2 * half; c < 2 * half + 2; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint64_t x2 = f2_fma(
-                f2_make(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])), sl2x2,
-                nbx2);
-            float x0, x1;
-            f2_split(x2, x0, x1);
-            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-            acc2[i & 1] = f2_add(acc2[i & 1], f2_make(p0, p1));
-            pk[i] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16(tS + c * 16, pk);
-        }
-        if (half == 0 && j > 0 && __any_sync(0xffffffffu, resc)) {
-          // PV(j-1) of this tile completed before S(j) was signalled.
+      const float inv_l = 1.0f / l;
+      const bool valid = q_idx < p.Sq;
+      __nv_bfloat16* orow_g = p.o + ((size_t)it.bh * p.Sq + (valid ? q_idx : 0)) * D;
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t orow[32];
-            tmem_ld32(tO + c * 32, orow);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-            tmem_st32(tO + c * 32, orow);
-          }
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t orow[32];
+        tmem_ld32(tO + c * 32, orow);
+        tmem_wait_ld();
+        if (c == D / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(bar(FB_OFREE + t));
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar((half == 0 ? FB_PFULL : FB_PFULL1) + t));
-      }
-      float a0, a1, a2, a3;
-      f2_split(acc2[0], a0, a1);
-      f2_split(acc2[1], a2, a3);
-      l = l * alpha + ((a0 + a1) + (a2 + a3));
-      m = m_use;
-    }
-    if (ok && nkv(t) > 0) {
-      ok = mbar_wait(bar(FB_ODONE + t), 0, abort_flag, 310 + t);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc_fence_after();
-        const float inv_l = 1.0f / l;
-        const bool valid = q_idx < p.Sq;
-        __nv_bfloat16* orow_g = p.o + ((size_t)bh * p.Sq + (valid ? q_idx : 0)) * D;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t orow[32];
-          tmem_ld32(tO + c * 32, orow);
-          tmem_wait_ld();
-          uint32_t w[16];
+        uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack_bf16x2(__uint_as_float(orow[2 * i]) * inv_l,
-                               __uint_as_float(orow[2 * i + 1]) * inv_l);
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(orow_g + c * 32);
+        for (int i = 0; i < 16; ++i)
+          w[i] = pack_bf16x2(__uint_as_float(orow[2 * i]) * inv_l,
+                             __uint_as_float(orow[2 * i + 1]) * inv_l);
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow_g + c * 32);
 #pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4)
-              dst[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
-          }
+          for (int v4 = 0; v4 < 4; ++v4)
+            dst[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
         }
-        if (valid) p.lse[(size_t)bh * p.Sq + q_idx] = (m + lg2_approx(l)) * 0.6931471805599453f;
       }
+      if (valid) p.lse[(size_t)it.bh * p.Sq + q_idx] = (m + lg2_approx(l)) * 0.6931471805599453f;
+      st_t += nk;
+      ++no_t;
     }
   }
 

@@ -205,7 +205,7 @@ extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const 
   prm.n_pairs = (int)n_pairs;
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
-  const dim3 grid((unsigned)(bhq * n_pairs));
+  const dim3 grid(persistent_grid(bhq * n_pairs));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128)
     fa_fwd_sm100_kernel<128><<<grid, FwdCfg<128>::kThreads, FwdCfg<128>::SMEM_BYTES, st>>>(
