@@ -44,6 +44,7 @@ struct FwdParams {
   int n_pairs;
   float scale_log2;  // softmax_scale * log2(e)
   int causal;
+  int heavy_first;  // item order: all heads' heaviest pairs first (K/V fit in L2)
 };
 
 template <int D>
@@ -85,17 +86,26 @@ __device__ __forceinline__ void mbar_drain_wait(uint32_t bar, uint32_t parity, i
   (void)mbar_wait(bar, parity, nullptr, site);
 }
 
-// Work item w = query-tile pair of one head: head-major (the CTAs running at
-// any time share a few heads' K/V in L2), heavy (late) pairs first within a
-// head when causal.  Each role derives the same values from w.
+// Work item w = query-tile pair of one head.  Default order: head-major (the
+// CTAs running at any time share a few heads' K/V in L2), heavy (late) pairs
+// first within a head when causal.  With heavy_first (causal, and all K/V
+// small enough to stay in L2): pair-major from the heaviest pair down, so the
+// boustrophedon rounds approximate longest-first scheduling.  Each role
+// derives the same values from w.
 struct FwdItem {
   int bh, bh_kv, q0, nkv0, nkv1, n_iter;
 };
 __device__ __forceinline__ FwdItem fwd_item(const FwdParams& p, int w) {
   FwdItem it;
-  it.bh = w / p.n_pairs;
-  int pair = w % p.n_pairs;
-  if (p.causal) pair = p.n_pairs - 1 - pair;
+  int pair;
+  if (p.heavy_first) {
+    pair = p.n_pairs - 1 - w / p.BHq;
+    it.bh = w % p.BHq;
+  } else {
+    it.bh = w / p.n_pairs;
+    pair = w % p.n_pairs;
+    if (p.causal) pair = p.n_pairs - 1 - pair;
+  }
   const int b = it.bh / p.Hq, h = it.bh % p.Hq;
   it.bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
   it.q0 = pair * 256;
