@@ -203,8 +203,8 @@ extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const 
   prm.Hkv = n_heads_kv;
   prm.BHq = (int)bhq;
   prm.n_pairs = (int)n_pairs;
-  // causal with all of K and V within half of L2: longest-first item order
-  prm.heavy_first = (causal && 2LL * batch * n_heads_kv * n_ctx_k * head_dim * 2 <= (64LL << 20)) ? 1 : 0;
+  // causal with all of K and V within the L2 size (126 MB): longest-first item order
+  prm.heavy_first = (causal && 2LL * batch * n_heads_kv * n_ctx_k * head_dim * 2 <= (128LL << 20)) ? 1 : 0;
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   const dim3 grid(persistent_grid(bhq * n_pairs));
