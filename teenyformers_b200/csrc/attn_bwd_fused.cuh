@@ -130,16 +130,22 @@ __device__ __forceinline__ constexpr uint32_t packed_col64(int kk) {
   return uint32_t((kk >> 2) * 64 + (kk & 3) * 8);
 }
 
-// Work item w = one 128-key tile of one KV head, head-major (a head's Q/dO
-// stay hot in L2 while its key tiles run), key tile 0 first within a head
-// (the most query tiles when causal).
+// Work item w = one 128-key tile of one KV head.  Items go in groups of
+// kItemHeadGroup KV heads (their Q/dO and dQ accumulator stay hot in L2 while
+// the group runs); within a group key-tile-major, key tile 0 first (the most
+// query tiles when causal), so the items handed out last are the lightest.
+constexpr int kItemHeadGroup = 8;
 struct FusedItem {
   int bh_kv, b, hk, k0, qt_first, qt_per_head, n_tiles;
 };
 __device__ __forceinline__ FusedItem fused_item(const BwdParams& p, int w) {
   FusedItem it;
-  it.bh_kv = w / p.n_kt;
-  const int kt = w % p.n_kt;
+  const int per_group = kItemHeadGroup * p.n_kt;
+  const int h0 = (w / per_group) * kItemHeadGroup;
+  const int gs = min(kItemHeadGroup, p.BHkv - h0);  // heads in this group
+  const int local = w - h0 * p.n_kt;
+  const int kt = local / gs;
+  it.bh_kv = h0 + local % gs;
   it.b = it.bh_kv / p.Hkv;
   it.hk = it.bh_kv % p.Hkv;
   it.k0 = kt * 128;
