@@ -531,43 +531,71 @@ def main():
     clocks = sampler.stop() if rank == 0 else None
 
     # ---- end to end through the public API, host buffers ----
+    # Pinned host Q, K, V, dO in, O, LSE, dQ, dK, dV out, every step.  The
+    # heads go in chunks over three streams (copy in / compute / copy out) so
+    # PCIe transfers in both directions overlap each other and the kernels,
+    # as a caller of flash_attn2_fwd/bwd would pipeline them.  Each step is
+    # timed from its first upload to its last download.
     e2e = None
     if not args.no_e2e:
         hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
-        outs_h = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (o, lse, dq, dk, dv)]
+        outs_d = (o, lse, dq, dk, dv)
+        outs_h = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs_d]
         n_e2e = max(3, min(args.steps, 10))
+        n_chunks = max(1, min(16, bh_local))
+        while bh_local % n_chunks:
+            n_chunks -= 1
+        hc = bh_local // n_chunks
+        s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        ws_c = tfb.bwd_workspace(q[:, :hc])
+        dev_in = (q, k, v, do)
 
         def e2e_step():
-            dq_, dk_, dv_ = (torch.empty_like(t, device=dev) for t in (q, k, v))
-            q_d = hq.to(dev, non_blocking=True)
-            k_d = hk.to(dev, non_blocking=True)
-            v_d = hv.to(dev, non_blocking=True)
-            do_d = hdo.to(dev, non_blocking=True)
-            o_d, lse_d = tfb.flash_attn2_fwd(q_d, k_d, v_d, scale, True)
-            grads = tfb.flash_attn2_bwd(q_d, k_d, v_d, o_d, lse_d, do_d, scale, True,
-                                        workspace=ws, grads=(dq_, dk_, dv_))
-            for h_t, d_t in zip(outs_h, (o_d, lse_d) + tuple(grads)):
-                h_t.copy_(d_t, non_blocking=True)
+            ev_start = torch.cuda.Event(enable_timing=True)
+            ev_end = torch.cuda.Event(enable_timing=True)
+            ev_start.record(s_in)
+            for c in range(n_chunks):
+                sl = slice(c * hc, (c + 1) * hc)
+                with torch.cuda.stream(s_in):
+                    for h_t, d_t in zip((hq, hk, hv, hdo), dev_in):
+                        d_t[:, sl].copy_(h_t[:, sl], non_blocking=True)
+                    e_in = torch.cuda.Event()
+                    e_in.record(s_in)
+                with torch.cuda.stream(s_cmp):
+                    s_cmp.wait_event(e_in)
+                    tfb.flash_attn2_fwd(q[:, sl], k[:, sl], v[:, sl], scale, True, out=o[:, sl],
+                                        lse=lse[:, sl])
+                    tfb.flash_attn2_bwd(q[:, sl], k[:, sl], v[:, sl], o[:, sl], lse[:, sl],
+                                        do[:, sl], scale, True, workspace=ws_c,
+                                        grads=(dq[:, sl], dk[:, sl], dv[:, sl]))
+                    e_cmp = torch.cuda.Event()
+                    e_cmp.record(s_cmp)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(e_cmp)
+                    for h_t, d_t in zip(outs_h, outs_d):
+                        h_t[:, sl].copy_(d_t[:, sl], non_blocking=True)
+            s_out.wait_stream(s_in)
+            ev_end.record(s_out)
+            return ev_start, ev_end
 
         e2e_step()
         torch.cuda.synchronize()
         barrier()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
+        t_ms = 0.0
         for _ in range(n_e2e):
-            e2e_step()
-        b.record(stream)
-        torch.cuda.synchronize()
+            e0, e1 = e2e_step()
+            torch.cuda.synchronize()
+            t_ms += e0.elapsed_time(e1)
         barrier()
-        e2e_ms = max_over_ranks(a.elapsed_time(b) / n_e2e)
+        e2e_ms = max_over_ranks(t_ms / n_e2e)
         h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo)) * world
         d2h = sum(t.numel() * t.element_size() for t in outs_h) * world
         e2e = {"value": (fwd_flops_total + bwd_flops_total) / (e2e_ms * 1e-3) / 1e12,
                "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": e2e_ms, "steps": n_e2e,
-               "path": "pinned host Q,K,V,dO -> flash_attn2_fwd/bwd (C ABI) -> pinned host "
-                       "O,LSE,dQ,dK,dV"}
+               "ms_per_step": e2e_ms, "steps": n_e2e, "chunks": n_chunks,
+               "path": "pinned host Q,K,V,dO -> flash_attn2_fwd/bwd (C ABI) on "
+                       f"{n_chunks} head chunks, uploads / kernels / downloads on three "
+                       "streams -> pinned host O,LSE,dQ,dK,dV"}
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
