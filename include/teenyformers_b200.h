@@ -227,6 +227,48 @@ TF_API int tf_b200_rmsnorm_bf16(const void* x, const void* residual, const void*
  *   z [rows, 2*d_ff] = [gate || up] bf16 -> out[m, n] = silu(gate[m, n]) * up[m, n], [rows, d_ff]. */
 TF_API int tf_b200_swiglu_bf16(const void* z, void* out, int rows, int d_ff, void* stream);
 
+/* ---------------- GEMMs of the Llama block with fused epilogues (tcgen05) ----------------
+ * C = A * B^T with bf16 operands and fp32 accumulation; B is an nn.Linear-style weight
+ * [n, k] (row-major).  These replace the teeny-core Linear calls of the attention layer
+ * and the FFN (src/layers/attention.rs:83-148, src/layers/ffn.rs:47-56), fused with the
+ * kernel that follows each one in src/layers/llama_block.rs:55-65.  Shape rules:
+ * k >= 1, k % 8 == 0, n % 8 == 0, 16-byte aligned pointers; m == 0 or n == 0 is a no-op.
+ *
+ * A operand: row-major [m, k], or, with a_seq > 0, the attention output
+ * [m / a_seq, k / 128, a_seq, 128] read as the [m, k] matrix MergeHeads would build
+ * (transpose_heads.rs:86-95 folded into the GEMM's loads; a_seq % 128 == 0). */
+TF_API int tf_b200_gemm_bf16(const void* a, const void* b, void* c, int m, int n, int k,
+                             int a_seq, void* stream);
+/* FFN gate/up projection + SwiGLU (swiglu.rs:56-95): w_gate_up is [2*d_ff, k] with gate and
+ * up rows interleaved in 128-row blocks (block 2j = gate rows 128j.., block 2j+1 = up rows
+ * 128j..); out [m, d_ff] = silu(a w_gate^T) * (a w_up^T).  d_ff % 128 == 0. */
+TF_API int tf_b200_gemm_swiglu_bf16(const void* a, const void* w_gate_up, void* out, int m,
+                                    int d_ff, int k, void* stream);
+/* (cos, sin) table [seq_len, head_dim / 2] of float pairs for the QKV epilogue, with the
+ * angles of tf_b200_rope_bf16 (rope.rs:86-93). */
+TF_API int tf_b200_rope_table_f32(void* cs, int seq_len, int head_dim, float ln_rope_base,
+                                  void* stream);
+/* QKV projection + TransposeHeads + RoPE (attention.rs:89-123) in one kernel:
+ * x [batch * seq_len, d_model], w_qkv = [Wq; Wk; Wv] [(n_heads_q + 2 n_heads_kv) * 128, d_model];
+ * q [batch, n_heads_q, seq_len, 128], k_out / v [batch, n_heads_kv, seq_len, 128].  Q and K are
+ * rotated with rope_cs (tf_b200_rope_table_f32; NULL = no rotation), style 0 = interleaved pairs,
+ * 1 = rotate-half.  head_dim is 128; seq_len % 128 == 0. */
+TF_API int tf_b200_gemm_qkv_rope_bf16(const void* x, const void* w_qkv, void* q, void* k_out,
+                                      void* v, const void* rope_cs, int batch, int seq_len,
+                                      int n_heads_q, int n_heads_kv, int d_model, int rope_style,
+                                      void* stream);
+/* Tensor-parallel o_proj / down_proj fused with the reduce-scatter half of the all-reduce
+ * that follows it (llama_block.rs:55-65 split over `world` ranks): the partial product's rows
+ * [o * m / world, (o + 1) * m / world) are stored straight into rank o's receive buffer
+ * peer_recv[o] (a host array of `world` device pointers, each [world, m / world, n]) at slot
+ * [rank], with NVLink peer stores as tiles finish.  The caller then runs
+ * tf_b200_allreduce_residual_rmsnorm_bf16 with peer_src[p] = its own receive buffer + (p - rank)
+ * * (m / world) * n elements (so global row r of slot p is at peer_src[p] + r * n), which sums
+ * local memory only.
+ * (m / world) % 128 == 0; world <= 8. */
+TF_API int tf_b200_gemm_push_bf16(const void* a, const void* b, void* const* peer_recv, int m,
+                                  int n, int k, int a_seq, int rank, int world, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -130,6 +130,23 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// (cos, sin) of every (position s, pair k) with the angle arithmetic of
+// rope_rows_kernel: cs[s * half + k] = (cos, sin)(s * exp(k * coef)).  The
+// GEMM epilogue that applies RoPE reads this table.
+__global__ void __launch_bounds__(256)
+    rope_table_kernel(float2* __restrict__ cs, int S, int half, float coef) {
+  const long long total = (long long)S * half;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int s = (int)(i / half), k = (int)(i % half);
+    const float inv_freq = expf((float)k * coef);
+    const float theta = (float)s * inv_freq;
+    float sv, cv;
+    sincosf(theta, &sv, &cv);
+    cs[i] = make_float2(cv, sv);
+  }
+}
+
 // Pure copy between [B,S,H,D] and [B,H,S,D] (either direction), any element
 // size: bit-exact.  VEC = bytes moved per access (16, 8, 4, 2 or 1).
 template <typename V>

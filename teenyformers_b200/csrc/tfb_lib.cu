@@ -25,6 +25,7 @@
 #include "rope_transpose.cuh"
 #include "norm_act.cuh"
 #include "comm_norm.cuh"
+#include "gemm_sm100.cuh"
 
 using namespace tfb;
 
@@ -86,6 +87,23 @@ bool make_f32_acc_map(CUtensorMap* map, const void* base, int D, long long rows)
   return r == CUDA_SUCCESS;
 }
 
+// 2-D bf16 tensor map over a row-major [rows, inner] matrix, (64 x box_rows)
+// box, 128-byte swizzle (the GEMM operand k-blocks).
+bool make_bf16_2d_map(CUtensorMap* map, const void* base, long long inner, long long rows,
+                      int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
@@ -117,6 +135,10 @@ int ensure_device_setup() {
     set((const void*)fa_bwd_fused_sm100_kernel<128>, BwdFusedCfg<128>::SMEM_BYTES);
     set((const void*)fa_decode_kernel<64>, DecCfg<64>::SMEM_BYTES);
     set((const void*)fa_decode_kernel<128>, DecCfg<128>::SMEM_BYTES);
+    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_STORE>, GemmCfg::SMEM_ALLOC);
+    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_SWIGLU>, GemmCfg::SMEM_ALLOC);
+    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_QKV_ROPE>, GemmCfg::SMEM_ALLOC);
+    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_PUSH>, GemmCfg::SMEM_ALLOC);
     const int f32_max = (3 * kF32Rows + 3 * kF32Tile) * kF32MaxD * 4 + 2 * kF32Tile * 4;
     set((const void*)fa_fwd_f32_kernel, f32_max);
     set((const void*)fa_bwd_dq_f32_kernel, f32_max);
@@ -687,6 +709,157 @@ extern "C" int tf_b200_swiglu_bf16(const void* z, void* out, int rows, int d_ff,
                                                        static_cast<__nv_bfloat16*>(out), rows,
                                                        d_ff);
   return launch_status();
+}
+
+// ===================================================================== GEMMs with fused epilogues
+namespace {
+
+// Shared validation + launch of gemm_bf16_sm100_kernel.  A is row-major
+// [m, k], or (a_seq > 0) the attention output [m / a_seq, k / 128, a_seq, 128].
+template <int EPI>
+int gemm_launch(const void* a, const void* b, int m, int n, int k, int a_seq, GemmParams& prm,
+                cudaStream_t st) {
+  if (!a || !b) return TF_ERR_INVALID_ARG;
+  if (k % 8 != 0 || n % 8 != 0) return TF_ERR_UNSUPPORTED;
+  if (!is_aligned(a, 16) || !is_aligned(b, 16)) return TF_ERR_MISALIGNED;
+  if (a_seq < 0) return TF_ERR_INVALID_ARG;
+  if (a_seq > 0 && (k % kGemmHeadDim != 0 || a_seq % kGemmBM != 0 || m % a_seq != 0))
+    return TF_ERR_UNSUPPORTED;
+  if (ensure_device_setup() != TF_OK) return TF_ERR_CUDA;
+  CUtensorMap ta, tb;
+  bool ok;
+  if (a_seq > 0) {
+    const long long outer = (long long)(m / a_seq) * (k / kGemmHeadDim);
+    if (!fits_i32(outer)) return TF_ERR_TOO_LARGE;
+    ok = make_bf16_map(&ta, a, kGemmHeadDim, a_seq, (int)outer, kGemmBM);
+  } else {
+    ok = make_bf16_2d_map(&ta, a, k, m, kGemmBM);
+  }
+  if (!ok || !make_bf16_2d_map(&tb, b, k, n, kGemmBN)) return TF_ERR_CUDA;
+  prm.M = m, prm.N = n, prm.K = k;
+  prm.n_mblk = (m + kGemmBM - 1) / kGemmBM;
+  prm.n_nblk = (n + kGemmBN - 1) / kGemmBN;
+  prm.n_kblk = (k + kGemmBK - 1) / kGemmBK;
+  const long long tiles = (long long)prm.n_mblk * prm.n_nblk;
+  if (!fits_i32(tiles)) return TF_ERR_TOO_LARGE;
+  prm.n_tiles = (int)tiles;
+  prm.group_m = std::min(prm.n_mblk, 16);
+  prm.a_heads = a_seq > 0 ? 1 : 0;
+  prm.a_seq = a_seq > 0 ? a_seq : 1;
+  prm.a_n_heads = a_seq > 0 ? k / kGemmHeadDim : 0;
+  gemm_bf16_sm100_kernel<EPI>
+      <<<persistent_grid(tiles), kGemmThreads, GemmCfg::SMEM_ALLOC, st>>>(ta, tb, prm);
+  return launch_status();
+}
+
+bool gemm_extents(int m, int n, int k, int* early) {
+  *early = TF_OK;
+  if (m < 0 || n < 0 || k < 0) {
+    *early = TF_ERR_INVALID_ARG;
+    return false;
+  }
+  if (m == 0 || n == 0) return false;  // nothing to write: a successful no-op
+  if (k == 0) {
+    *early = TF_ERR_UNSUPPORTED;
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+extern "C" int tf_b200_gemm_bf16(const void* a, const void* b, void* c, int m, int n, int k,
+                                 int a_seq, void* stream) {
+  int early;
+  if (!gemm_extents(m, n, k, &early)) return early;
+  if (!c) return TF_ERR_INVALID_ARG;
+  if (!is_aligned(c, 16)) return TF_ERR_MISALIGNED;
+  GemmParams prm{};
+  prm.out = static_cast<__nv_bfloat16*>(c);
+  prm.ld_out = n;
+  return gemm_launch<GEMM_EPI_STORE>(a, b, m, n, k, a_seq, prm,
+                                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_b200_gemm_swiglu_bf16(const void* a, const void* w_gate_up, void* out, int m,
+                                        int d_ff, int k, void* stream) {
+  int early;
+  if (d_ff < 0) return TF_ERR_INVALID_ARG;
+  if (!gemm_extents(m, d_ff, k, &early)) return early;
+  if (!out) return TF_ERR_INVALID_ARG;
+  if (d_ff % 128 != 0 || !fits_i32(2LL * d_ff)) return TF_ERR_UNSUPPORTED;
+  if (!is_aligned(out, 16)) return TF_ERR_MISALIGNED;
+  GemmParams prm{};
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.ld_out = d_ff;
+  return gemm_launch<GEMM_EPI_SWIGLU>(a, w_gate_up, m, 2 * d_ff, k, 0, prm,
+                                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_b200_rope_table_f32(void* cs, int seq_len, int head_dim, float ln_rope_base,
+                                      void* stream) {
+  if (seq_len < 0 || head_dim < 0) return TF_ERR_INVALID_ARG;
+  if (seq_len == 0 || head_dim == 0) return TF_OK;
+  if (!cs || head_dim % 2 != 0) return TF_ERR_INVALID_ARG;
+  if (!is_aligned(cs, 16)) return TF_ERR_MISALIGNED;
+  if (!std::isfinite(ln_rope_base)) return TF_ERR_INVALID_ARG;
+  const long long total = (long long)seq_len * (head_dim / 2);
+  const long long blocks = (total + 255) / 256;
+  const float coef = (-2.0f * ln_rope_base) / (float)head_dim;
+  rope_table_kernel<<<(unsigned)std::min(blocks, 148LL * 8), 256, 0,
+                      static_cast<cudaStream_t>(stream)>>>(static_cast<float2*>(cs), seq_len,
+                                                           head_dim / 2, coef);
+  return launch_status();
+}
+
+extern "C" int tf_b200_gemm_qkv_rope_bf16(const void* x, const void* w_qkv, void* q, void* k_out,
+                                          void* v, const void* rope_cs, int batch, int seq_len,
+                                          int n_heads_q, int n_heads_kv, int d_model,
+                                          int rope_style, void* stream) {
+  if (batch < 0 || seq_len < 0 || n_heads_q < 0 || n_heads_kv < 0 || d_model < 0)
+    return TF_ERR_INVALID_ARG;
+  const long long m = (long long)batch * seq_len;
+  const long long n = (long long)(n_heads_q + 2LL * n_heads_kv) * kGemmHeadDim;
+  if (!fits_i32(m) || !fits_i32(n)) return TF_ERR_TOO_LARGE;
+  int early;
+  if (!gemm_extents((int)m, (int)n, d_model, &early)) return early;
+  if (!q || (n_heads_kv > 0 && (!k_out || !v))) return TF_ERR_INVALID_ARG;
+  if (rope_style != 0 && rope_style != 1) return TF_ERR_INVALID_ARG;
+  if (seq_len % kGemmBM != 0) return TF_ERR_UNSUPPORTED;
+  if (!is_aligned(q, 16) || (k_out && !is_aligned(k_out, 16)) || (v && !is_aligned(v, 16)) ||
+      (rope_cs && !is_aligned(rope_cs, 16)))
+    return TF_ERR_MISALIGNED;
+  GemmParams prm{};
+  prm.q_out = static_cast<__nv_bfloat16*>(q);
+  prm.k_out = static_cast<__nv_bfloat16*>(k_out);
+  prm.v_out = static_cast<__nv_bfloat16*>(v);
+  prm.rope_cs = static_cast<const float4*>(rope_cs);
+  prm.seq = seq_len;
+  prm.n_q_heads = n_heads_q;
+  prm.n_kv_heads = n_heads_kv;
+  prm.rope_style = rope_style;
+  return gemm_launch<GEMM_EPI_QKV_ROPE>(x, w_qkv, (int)m, (int)n, d_model, 0, prm,
+                                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tf_b200_gemm_push_bf16(const void* a, const void* b, void* const* peer_recv,
+                                      int m, int n, int k, int a_seq, int rank, int world,
+                                      void* stream) {
+  int early;
+  if (!gemm_extents(m, n, k, &early)) return early;
+  if (!peer_recv || world < 1 || world > kGemmMaxPeers || rank < 0 || rank >= world)
+    return TF_ERR_INVALID_ARG;
+  if (m % world != 0 || (m / world) % kGemmBM != 0) return TF_ERR_UNSUPPORTED;
+  GemmParams prm{};
+  for (int r = 0; r < world; ++r) {
+    if (!peer_recv[r]) return TF_ERR_INVALID_ARG;
+    if (!is_aligned(peer_recv[r], 16)) return TF_ERR_MISALIGNED;
+    prm.peer_out[r] = static_cast<__nv_bfloat16*>(peer_recv[r]);
+  }
+  prm.rank = rank;
+  prm.world = world;
+  prm.slice_rows = m / world;
+  return gemm_launch<GEMM_EPI_PUSH>(a, b, m, n, k, a_seq, prm, static_cast<cudaStream_t>(stream));
 }
 
 // ===================================================================== backward, no scratch argument

@@ -30,7 +30,8 @@ __all__ = [
     "FlashAttn2Op", "CausalFlashAttn2Op", "RopeOp", "TransposeHeadsOp", "MergeHeadsOp",
     "flash_attn2_fwd", "flash_attn2_bwd", "rope", "rope_transpose", "transpose_heads",
     "merge_heads", "bwd_workspace", "rmsnorm", "swiglu", "flash_attn2_decode",
-    "decode_workspace", "TF_ROPE_INTERLEAVED",
+    "decode_workspace", "linear", "linear_swiglu", "swiglu_weight_blocks", "rope_table",
+    "linear_qkv_rope", "linear_push", "TF_ROPE_INTERLEAVED",
     "TF_ROPE_ROTATE_HALF", "TfError",
 ]
 
@@ -231,6 +232,110 @@ def swiglu(z: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     y = torch.empty(z.shape[:-1] + (d_ff,), dtype=z.dtype, device=z.device) if out is None else out
     call("tf_b200_swiglu_bf16", _ptr(z), _ptr(y), rows, d_ff, _stream(z))
     return y
+
+
+def _bf16(*ts):
+    for t in ts:
+        _need(t.is_cuda and t.is_contiguous() and t.dtype == torch.bfloat16,
+              "GEMM tensors must be contiguous bf16 CUDA tensors")
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
+           heads_seq: int = 0) -> torch.Tensor:
+    """x @ weight.T on the tcgen05 GEMM (teeny-core Linear in the block).
+
+    x: [..., k] row-major, or (heads_seq > 0) the attention output
+    [B, H, heads_seq, 128], read as the [B * heads_seq, H * 128] matrix that
+    merge_heads would build.  weight: [n, k].  Returns [..., n] (or
+    [B, heads_seq, n])."""
+    _bf16(x, weight)
+    n, k = weight.shape
+    if heads_seq > 0:
+        _need(x.dim() == 4 and x.shape[2] == heads_seq and x.shape[1] * x.shape[3] == k,
+              "heads-layout x must be [B, H, S, 128] with H * 128 == k")
+        lead = (x.shape[0], heads_seq)
+        m = x.shape[0] * heads_seq
+    else:
+        _need(x.shape[-1] == k, "x's last dim must match weight's k")
+        lead = tuple(x.shape[:-1])
+        m = x.numel() // max(k, 1)
+    y = torch.empty(lead + (n,), dtype=x.dtype, device=x.device) if out is None else out
+    _bf16(y)
+    _need(y.numel() == m * n, "out has the wrong size")
+    call("tf_b200_gemm_bf16", _ptr(x), _ptr(weight), _ptr(y), m, n, k, int(heads_seq),
+         _stream(x))
+    return y
+
+
+def swiglu_weight_blocks(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[d_ff, k] gate and up weights -> the [2 d_ff, k] block-interleaved weight
+    linear_swiglu reads (128-row blocks: gate 0, up 0, gate 1, up 1, ...)."""
+    d_ff, k = w_gate.shape
+    _need(w_up.shape == w_gate.shape and d_ff % 128 == 0, "gate/up must be [d_ff, k], d_ff % 128 == 0")
+    return torch.stack([w_gate.reshape(d_ff // 128, 128, k), w_up.reshape(d_ff // 128, 128, k)],
+                       dim=1).reshape(2 * d_ff, k).contiguous()
+
+
+def linear_swiglu(x: torch.Tensor, w_gate_up_blocks: torch.Tensor,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(x @ w_gate.T) * (x @ w_up.T) in one GEMM (ffn.rs:47-56 + swiglu.rs:56-95);
+    the weight comes from swiglu_weight_blocks."""
+    _bf16(x, w_gate_up_blocks)
+    n2, k = w_gate_up_blocks.shape
+    d_ff = n2 // 2
+    _need(x.shape[-1] == k, "x's last dim must match the weight's k")
+    m = x.numel() // max(k, 1)
+    y = torch.empty(tuple(x.shape[:-1]) + (d_ff,), dtype=x.dtype, device=x.device) if out is None else out
+    _bf16(y)
+    _need(y.numel() == m * d_ff, "out has the wrong size")
+    call("tf_b200_gemm_swiglu_bf16", _ptr(x), _ptr(w_gate_up_blocks), _ptr(y), m, d_ff, k,
+         _stream(x))
+    return y
+
+
+def rope_table(seq_len: int, head_dim: int, rope_base: float, device) -> torch.Tensor:
+    """[seq_len, head_dim / 2, 2] fp32 (cos, sin) table for linear_qkv_rope."""
+    t = torch.empty((seq_len, head_dim // 2, 2), dtype=torch.float32, device=device)
+    call("tf_b200_rope_table_f32", _ptr(t), seq_len, head_dim, float(math.log(rope_base)),
+         ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream))
+    return t
+
+
+def linear_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, n_heads_q: int, n_heads_kv: int,
+                    table: torch.Tensor | None, style: int = TF_ROPE_INTERLEAVED, outs=None):
+    """x [B, S, d] @ [Wq; Wk; Wv].T -> (q [B, Hq, S, 128], k, v [B, Hkv, S, 128]) with RoPE
+    on q and k (attention.rs:89-123: projections, TransposeHeads, RoPE) in one kernel."""
+    _bf16(x, w_qkv)
+    B, S, d = x.shape
+    D = 128
+    _need(w_qkv.shape == ((n_heads_q + 2 * n_heads_kv) * D, d), "w_qkv shape mismatch")
+    if outs is None:
+        outs = (torch.empty((B, n_heads_q, S, D), dtype=x.dtype, device=x.device),
+                torch.empty((B, n_heads_kv, S, D), dtype=x.dtype, device=x.device),
+                torch.empty((B, n_heads_kv, S, D), dtype=x.dtype, device=x.device))
+    q, k, v = outs
+    _bf16(q, k, v)
+    if table is not None:
+        _need(table.is_cuda and table.dtype == torch.float32 and table.is_contiguous()
+              and table.shape[0] >= S and table.numel() // table.shape[0] == D,
+              "table must be a contiguous fp32 [>= S, 64, 2] CUDA tensor")
+    call("tf_b200_gemm_qkv_rope_bf16", _ptr(x), _ptr(w_qkv), _ptr(q), _ptr(k), _ptr(v),
+         _ptr(table), B, S, n_heads_q, n_heads_kv, d, int(style), _stream(x))
+    return q, k, v
+
+
+def linear_push(x: torch.Tensor, weight: torch.Tensor, peer_recv_ptrs, rank: int, world: int,
+                heads_seq: int = 0) -> None:
+    """Tensor-parallel partial product x @ weight.T whose row slice o is stored
+    into rank o's receive buffer peer_recv_ptrs[o] at slot [rank]
+    ([world, m / world, n] each): the reduce-scatter half of the all-reduce that
+    follows o_proj / down_proj, fused into the GEMM."""
+    _bf16(x, weight)
+    n, k = weight.shape
+    m = (x.shape[0] * heads_seq) if heads_seq > 0 else x.numel() // max(k, 1)
+    arr = (ctypes.c_void_p * world)(*[int(p) for p in peer_recv_ptrs])
+    call("tf_b200_gemm_push_bf16", _ptr(x), _ptr(weight), arr, m, n, k, int(heads_seq), rank,
+         world, _stream(x))
 
 
 # ----------------------------------------------------------------- op classes

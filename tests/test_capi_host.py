@@ -97,6 +97,36 @@ def test_rope_and_transpose_reject_bad_arguments(native_lib):
     assert _capi.raw("tf_b200_merge_heads", FAKE, None, 1, 4, 2, 8, 2, None) == TF_ERR_INVALID_ARG
 
 
+def test_gemm_entries_reject_bad_arguments(native_lib):
+    g = lambda *a: _capi.raw("tf_b200_gemm_bf16", *a, None)
+    assert g(FAKE, FAKE, FAKE, -1, 256, 64, 0) == TF_ERR_INVALID_ARG
+    assert g(FAKE, FAKE, FAKE, 0, 256, 64, 0) == TF_OK          # empty output: no-op
+    assert g(FAKE, FAKE, FAKE, 128, 256, 0, 0) == TF_ERR_UNSUPPORTED
+    assert g(FAKE, FAKE, FAKE, 128, 256, 60, 0) == TF_ERR_UNSUPPORTED   # k % 8
+    assert g(FAKE, FAKE, FAKE, 128, 250, 64, 0) == TF_ERR_UNSUPPORTED   # n % 8
+    assert g(None, FAKE, FAKE, 128, 256, 64, 0) == TF_ERR_INVALID_ARG
+    assert g(FAKE, FAKE, ODD, 128, 256, 64, 0) == TF_ERR_MISALIGNED
+    assert g(FAKE, FAKE, FAKE, 256, 256, 192, 128) == TF_ERR_UNSUPPORTED  # heads layout: k % 128
+    assert g(FAKE, FAKE, FAKE, 384, 256, 256, 256) == TF_ERR_UNSUPPORTED  # m % a_seq
+    sw = lambda *a: _capi.raw("tf_b200_gemm_swiglu_bf16", *a, None)
+    assert sw(FAKE, FAKE, FAKE, 128, 200, 64) == TF_ERR_UNSUPPORTED      # d_ff % 128
+    assert sw(FAKE, FAKE, None, 128, 256, 64) == TF_ERR_INVALID_ARG
+    qkv = lambda *a: _capi.raw("tf_b200_gemm_qkv_rope_bf16", *a, None)
+    assert qkv(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 200, 2, 1, 256, 0) == TF_ERR_UNSUPPORTED
+    assert qkv(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 256, 2, 1, 256, 5) == TF_ERR_INVALID_ARG
+    assert qkv(FAKE, FAKE, FAKE, None, FAKE, FAKE, 1, 256, 2, 1, 256, 0) == TF_ERR_INVALID_ARG
+    assert qkv(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 256, 2, 1, 256, 0) == TF_OK
+    assert _capi.raw("tf_b200_rope_table_f32", FAKE, 16, 7, 9.2, None) == TF_ERR_INVALID_ARG
+    peers = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+    push = lambda *a: _capi.raw("tf_b200_gemm_push_bf16", *a, None)
+    assert push(FAKE, FAKE, peers, 512, 256, 64, 0, 0, 9) == TF_ERR_INVALID_ARG   # world > 8
+    assert push(FAKE, FAKE, peers, 512, 256, 64, 0, 2, 2) == TF_ERR_INVALID_ARG   # rank
+    assert push(FAKE, FAKE, peers, 384, 256, 64, 0, 0, 2) == TF_ERR_UNSUPPORTED   # slice % 128
+    assert push(FAKE, FAKE, None, 512, 256, 64, 0, 0, 2) == TF_ERR_INVALID_ARG
+    odd = (ctypes.c_void_p * 2)(0x10000, 0x20002)
+    assert push(FAKE, FAKE, odd, 512, 256, 64, 0, 0, 2) == TF_ERR_MISALIGNED
+
+
 def test_op_shape_inference_mirrors_reference():
     from teenyformers_b200 import (CausalFlashAttn2Op, FlashAttn2Op, MergeHeadsOp, RopeOp,
                                    TransposeHeadsOp)
