@@ -303,7 +303,7 @@ def tfb_status() -> int:
 
 def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
     """Config #5: one Llama-3-8B-shaped decoder layer prefill, tensor-parallel
-    over the ranks (NCCL all-reduce after o_proj and down_proj)."""
+    over the ranks (all-reduce after o_proj and down_proj)."""
     import torch
     import torch.distributed as dist
 
@@ -339,20 +339,33 @@ def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
     if world > 1:
         from teenyformers_b200.tp import PeerAllReduceNorm
         peer = PeerAllReduceNorm(tokens, c["d_model"], device=dev)
-        ms_nccl = measure(LlamaLayerTP(cfg, w, world=world,
+        ms_nccl = measure(LlamaLayerTP(cfg, w, world=world, fused=False,
                                        all_reduce=lambda t: dist.all_reduce(t)))
-        ms = measure(LlamaLayerTP(cfg, w, world=world, peer_ar=peer))
+        ms_peer = measure(LlamaLayerTP(cfg, w, world=world, peer_ar=peer, fused=False))
+        layer = LlamaLayerTP(cfg, w, world=world, peer_ar=peer)
+        assert layer.fused_ok(c["batch"], c["seq"])
+        ms = measure(layer)
         res["nccl_allreduce_ms_per_step"] = ms_nccl
         res["nccl_allreduce_tflops"] = flops / (ms_nccl * 1e-3) / 1e12
-        collective = ("all-reduce + residual + RMSNorm fused in one kernel over NVLink peer "
-                      "memory (this library); nccl_* = the same layer with NCCL all-reduces")
+        res["unfused_peer_ms_per_step"] = ms_peer
+        collective = ("o_proj / down_proj GEMMs push their row slices to the owner ranks over "
+                      "NVLink (reduce-scatter overlapped with the GEMM), then one kernel sums the "
+                      "slices + residual, all-gathers h with peer stores and applies RMSNorm; "
+                      "nccl_* = cuBLAS projections + separate kernels + NCCL all-reduces; "
+                      "unfused_peer_* = the same with the peer all-reduce kernel")
         launches = 8
     else:
-        ms = measure(LlamaLayerTP(cfg, w, world=world))
-        collective = "no collective at TP x1"
-        launches = 8
+        ms_unfused = measure(LlamaLayerTP(cfg, w, world=world, fused=False))
+        layer = LlamaLayerTP(cfg, w, world=world)
+        assert layer.fused_ok(c["batch"], c["seq"])
+        ms = measure(layer)
+        res["unfused_ms_per_step"] = ms_unfused
+        res["unfused_tflops"] = flops / (ms_unfused * 1e-3) / 1e12
+        collective = ("no collective at TP x1; unfused_* = cuBLAS projections + separate "
+                      "RoPE/transpose, merge, SwiGLU and residual-add kernels")
+        launches = 7
     tf = flops / (ms * 1e-3) / 1e12
-    del w, x
+    del w, x, layer
     res["device_status"] = tfb_status()
     res.update({"tflops": tf, "tokens_per_s": tokens / (ms * 1e-3), "ms_per_step": ms,
                 "steps": n, "flops_per_step": flops,
@@ -360,8 +373,10 @@ def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
                 "launches_per_step_ours": launches,
                 "workload": f"config#5 Llama-3-8B-shaped layer prefill B{c['batch']} S{c['seq']} "
                             f"d{c['d_model']} H{c['heads']}/{c['kv_heads']} ff{c['d_ff']}, "
-                            f"TP x{world}; RMSNorm/RoPE+transpose/attention/merge/SwiGLU on this "
-                            "library's kernels, projections cuBLAS bf16; " + collective})
+                            f"TP x{world}; every kernel from this library: RMSNorm, QKV GEMM "
+                            "with RoPE + head transpose in its epilogue, causal attention, "
+                            "o_proj GEMM reading the attention layout, gate/up GEMM with "
+                            "SwiGLU epilogue, down GEMM; " + collective})
     return res
 
 

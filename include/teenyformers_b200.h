@@ -236,9 +236,11 @@ TF_API int tf_b200_swiglu_bf16(const void* z, void* out, int rows, int d_ff, voi
  *
  * A operand: row-major [m, k], or, with a_seq > 0, the attention output
  * [m / a_seq, k / 128, a_seq, 128] read as the [m, k] matrix MergeHeads would build
- * (transpose_heads.rs:86-95 folded into the GEMM's loads; a_seq % 128 == 0). */
-TF_API int tf_b200_gemm_bf16(const void* a, const void* b, void* c, int m, int n, int k,
-                             int a_seq, void* stream);
+ * (transpose_heads.rs:86-95 folded into the GEMM's loads; a_seq % 128 == 0).
+ * residual: NULL, or a bf16 [m, n] added to the rounded product (c = bf16(a b^T) + residual,
+ * the layer's final residual add; c may alias residual). */
+TF_API int tf_b200_gemm_bf16(const void* a, const void* b, const void* residual, void* c, int m,
+                             int n, int k, int a_seq, void* stream);
 /* FFN gate/up projection + SwiGLU (swiglu.rs:56-95): w_gate_up is [2*d_ff, k] with gate and
  * up rows interleaved in 128-row blocks (block 2j = gate rows 128j.., block 2j+1 = up rows
  * 128j..); out [m, d_ff] = silu(a w_gate^T) * (a w_up^T).  d_ff % 128 == 0. */

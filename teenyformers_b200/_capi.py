@@ -48,7 +48,7 @@ SIGNATURES = {
     "tf_b200_merge_heads": (I, [P, P, I, I, I, I, I, P]),
     "tf_b200_rmsnorm_bf16": (I, [P, P, P, P, P, I, I, F, P]),
     "tf_b200_swiglu_bf16": (I, [P, P, I, I, P]),
-    "tf_b200_gemm_bf16": (I, [P, P, P, I, I, I, I, P]),
+    "tf_b200_gemm_bf16": (I, [P, P, P, P, I, I, I, I, P]),
     "tf_b200_gemm_swiglu_bf16": (I, [P, P, P, I, I, I, P]),
     "tf_b200_rope_table_f32": (I, [P, I, I, F, P]),
     "tf_b200_gemm_qkv_rope_bf16": (I, [P] * 6 + [I] * 6 + [P]),

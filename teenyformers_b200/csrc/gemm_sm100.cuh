@@ -11,7 +11,7 @@
 // (src/layers/attention.rs:83-148, src/layers/ffn.rs:47-56,
 // src/layers/llama_block.rs:55-65); the epilogues replace the kernels that
 // follow them:
-//   STORE      C = acc as bf16                                (Linear)
+//   STORE      C = acc as bf16 (+ a residual R: C = bf16(acc) + R)  (Linear)
 //   SWIGLU     B's rows hold gate and up interleaved in 128-row blocks
 //              (tile n = [gate rows 128n.. | up rows 128n..]);
 //              C[M, N/2] = silu(gate) * up                    (swiglu.rs:56-95)
@@ -88,9 +88,11 @@ struct GemmParams {
   // A in [B, H, S, 128] layout (a_heads = 1): A row m = (b, s) with
   // b = m / a_seq, column k = (h, d) with h = k / 128
   int a_heads, a_seq, a_n_heads;
-  // STORE / SWIGLU output, row stride ld_out elements
+  // STORE / SWIGLU output, row stride ld_out elements; STORE adds `residual`
+  // ([M, N], row stride ld_out) when it is non-null
   __nv_bfloat16* out;
   long long ld_out;
+  const __nv_bfloat16* residual;
   // QKV_ROPE: outputs [B, H, S, 128]; rope_cs = [seq, 64] (cos, sin) pairs or
   // null (no rotation); rope_style 0 = interleaved pairs, 1 = rotate-half
   __nv_bfloat16* q_out;
@@ -142,18 +144,29 @@ __device__ __forceinline__ void gemm_tile(const GemmParams& p, int t, int& mb, i
 __device__ __forceinline__ float gemm_silu(float g) { return g / (1.0f + __expf(-g)); }
 
 // Writes this warp's 32 staged rows of 64 bf16 (128 B each, 16-byte chunks
-// XOR-swizzled by row) to dst rows row0.. with row stride ld; rows >= row_end
-// and 8-column groups at or past col_end are skipped.
+// XOR-swizzled by row) to dst rows row0.. with row stride ld; rows at or past
+// rows_valid and 8-column groups at or past cols_valid are skipped.  With
+// res_row0, the same-shaped bf16 residual is added (fp32 add of the two bf16
+// values, rounded once more: what the unfused GEMM + add computes).
 __device__ __forceinline__ void gemm_store_rows64(uint32_t stg, __nv_bfloat16* dst_row0,
-                                                  long long ld, int lane, int rows_valid,
-                                                  int cols_valid) {
+                                                  const __nv_bfloat16* res_row0, long long ld,
+                                                  int lane, int rows_valid, int cols_valid) {
   const int jj = lane & 7;
 #pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int rr = it * 4 + (lane >> 3);
-    const uint4 v = gemm_lds128(stg + rr * 128 + ((jj ^ (rr & 7)) << 4));
-    if (rr < rows_valid && jj * 8 < cols_valid)
+    uint4 v = gemm_lds128(stg + rr * 128 + ((jj ^ (rr & 7)) << 4));
+    if (rr < rows_valid && jj * 8 < cols_valid) {
+      if (res_row0) {
+        float a[8], r[8];
+        bf16x8_to_f32(v, a);
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(res_row0 + (long long)rr * ld + jj * 8), r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[e] += r[e];
+        v = f32_to_bf16x8(a);
+      }
       *reinterpret_cast<uint4*>(dst_row0 + (long long)rr * ld + jj * 8) = v;
+    }
   }
 }
 
@@ -291,9 +304,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (EPI == GEMM_EPI_STORE || EPI == GEMM_EPI_PUSH) {
         long long ld;
         __nv_bfloat16* dst_row0;
+        const __nv_bfloat16* res_row0 = nullptr;
         if constexpr (EPI == GEMM_EPI_STORE) {
           ld = p.ld_out;
           dst_row0 = p.out + (long long)row0 * ld;
+          if (p.residual) res_row0 = p.residual + (long long)row0 * ld;
         } else {
           // rank `owner` keeps rows [owner * slice, (owner + 1) * slice); ours go
           // to its slot [rank] (rows rank * slice.. of its receive buffer)
@@ -324,7 +339,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           __syncwarp();
           const int col0 = nb * kGemmBN + c * 64;
-          gemm_store_rows64(sb, dst_row0 + col0, ld, lane, rows_valid, p.N - col0);
+          gemm_store_rows64(sb, dst_row0 + col0, res_row0 ? res_row0 + col0 : nullptr, ld, lane,
+                            rows_valid, p.N - col0);
           __syncwarp();
         }
       } else if constexpr (EPI == GEMM_EPI_SWIGLU) {
@@ -357,7 +373,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           __syncwarp();
           const int col0 = nb * 128 + c * 64;
-          gemm_store_rows64(sb, dst_row0 + col0, p.ld_out, lane, rows_valid, n_out - col0);
+          gemm_store_rows64(sb, dst_row0 + col0, nullptr, p.ld_out, lane, rows_valid,
+                            n_out - col0);
           __syncwarp();
         }
       } else {

@@ -768,15 +768,16 @@ bool gemm_extents(int m, int n, int k, int* early) {
 
 }  // namespace
 
-extern "C" int tf_b200_gemm_bf16(const void* a, const void* b, void* c, int m, int n, int k,
-                                 int a_seq, void* stream) {
+extern "C" int tf_b200_gemm_bf16(const void* a, const void* b, const void* residual, void* c,
+                                 int m, int n, int k, int a_seq, void* stream) {
   int early;
   if (!gemm_extents(m, n, k, &early)) return early;
   if (!c) return TF_ERR_INVALID_ARG;
-  if (!is_aligned(c, 16)) return TF_ERR_MISALIGNED;
+  if (!is_aligned(c, 16) || (residual && !is_aligned(residual, 16))) return TF_ERR_MISALIGNED;
   GemmParams prm{};
   prm.out = static_cast<__nv_bfloat16*>(c);
   prm.ld_out = n;
+  prm.residual = static_cast<const __nv_bfloat16*>(residual);
   return gemm_launch<GEMM_EPI_STORE>(a, b, m, n, k, a_seq, prm,
                                      static_cast<cudaStream_t>(stream));
 }

@@ -14,13 +14,28 @@ and ``MultiHeadAttention::forward`` (src/layers/attention.rs:83-148):
 The reference layer is MHA and single-device; this adds GQA and tensor
 parallelism (config #5): each of the N ranks owns Hq/N query heads, Hkv/N KV
 heads and d_ff/N FFN columns, so the only exchange is an all-reduce (sum) of
-the o_proj and down_proj partial outputs.  The attention pieces, RoPE +
-transpose, merge, RMSNorm (fused with the residual add) and SwiGLU run on
-this library's sm_100a kernels; the projections are plain bf16 GEMMs
-(torch.matmul -> cuBLAS).  The all-reduce is either NCCL through
-torch.distributed (`all_reduce`) or, with `peer_ar` (a tp.PeerAllReduceNorm),
-this library's kernel that does the all-reduce, the residual add and the
-RMSNorm in one pass over NVLink peer memory.
+the o_proj and down_proj partial outputs.
+
+Default (fused) path, all on this library's sm_100a kernels:
+    h        = RMSNorm(x)
+    q, k, v  = one tcgen05 GEMM whose epilogue applies RoPE and writes the
+               [B, H, S, 128] attention layout (transpose_heads folded in)
+    o        = causal flash attention
+    o_proj   = GEMM reading o in its own layout (merge_heads folded into the
+               loads); with N > 1 ranks its epilogue pushes each row slice to
+               the rank that owns it (the reduce-scatter, overlapped tile by
+               tile), then one kernel sums the slices + residual, all-gathers
+               h over NVLink and applies RMSNorm
+    a        = gate/up GEMM with SwiGLU in its epilogue
+    down     = GEMM; pushed like o_proj (N > 1) or with the residual add in its
+               epilogue (N = 1)
+The fused path needs head_dim 128 and S % 128 == 0 (and B*S a multiple of
+128 * N with the peer all-reduce); other shapes, or ``fused=False``, take the
+separate-kernel path: the projections are plain torch.matmul (cuBLAS) calls
+followed by the separate RoPE/transpose, merge and SwiGLU kernels, and the
+all-reduce is NCCL through torch.distributed (`all_reduce`) or, with
+`peer_ar` (a tp.PeerAllReduceNorm), this library's all-reduce + residual +
+RMSNorm kernel loading the partials over NVLink.
 """
 from __future__ import annotations
 
@@ -104,7 +119,7 @@ class LlamaLayerTP:
     the tensor-parallel group in place (identity for one rank)."""
 
     def __init__(self, cfg: LlamaLayerConfig, weights: dict, world: int = 1, all_reduce=None,
-                 peer_ar=None):
+                 peer_ar=None, fused: bool = True):
         if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.d_ff % world:
             raise ValueError("heads and d_ff must split evenly over the ranks")
         self.cfg = cfg
@@ -116,8 +131,57 @@ class LlamaLayerTP:
         self.all_reduce = all_reduce or (lambda t: t)
         self.peer_ar = peer_ar
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        # the fused epilogues are built for head_dim 128; sequences must be a
+        # multiple of 128 (checked per call, else the separate-kernel path runs)
+        self.fused = fused and cfg.head_dim == 128
+        self._tables = {}
+        if self.fused:
+            w = weights
+            self.w_qkv = torch.cat([w["wq"], w["wk"], w["wv"]]).contiguous()
+            gu = w["w_gate_up"]  # [gate shard; up shard]
+            self.w_gu_blocks = ops.swiglu_weight_blocks(gu[:self.ff], gu[self.ff:])
+
+    def _rope_table(self, S: int, device) -> torch.Tensor:
+        t = self._tables.get(S)
+        if t is None:
+            t = ops.rope_table(S, self.cfg.head_dim, self.cfg.rope_base, device)
+            self._tables[S] = t
+        return t
+
+    def _forward_fused(self, x: torch.Tensor) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        B, S, d = x.shape
+        h = ops.rmsnorm(x, w["norm1"], cfg.eps)
+        q, k, v = ops.linear_qkv_rope(h, self.w_qkv, self.hq, self.hkv,
+                                      self._rope_table(S, x.device), cfg.rope_style)
+        o, _ = ops.flash_attn2_fwd(q, k, v, self.scale, True)
+        if self.peer_ar is not None:
+            ar = self.peer_ar
+            ops.linear_push(o, w["wo"], ar.recv_ptrs, ar.rank, ar.world, heads_seq=S)
+            x2, h2 = ar(0, x, w["norm2"], cfg.eps, pushed=True)
+            a = ops.linear_swiglu(h2.view(B, S, d), self.w_gu_blocks)
+            ops.linear_push(a, w["w_down"], ar.recv_ptrs, ar.rank, ar.world)
+            out, _ = ar(1, x2, pushed=True)
+            return out.view(B, S, d)
+        attn = ops.linear(o, w["wo"], heads_seq=S)
+        self.all_reduce(attn)
+        h2, x2 = ops.rmsnorm(attn, w["norm2"], cfg.eps, residual=x)
+        a = ops.linear_swiglu(h2, self.w_gu_blocks)
+        if self.world == 1:
+            return ops.linear(a, w["w_down"], residual=x2)
+        f = ops.linear(a, w["w_down"])
+        self.all_reduce(f)
+        return x2 + f
+
+    def fused_ok(self, B: int, S: int) -> bool:
+        """Whether forward() takes the fused path for a [B, S, d] input."""
+        if not self.fused or S % 128:
+            return False
+        return self.peer_ar is None or (B * S) % (128 * self.world) == 0
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fused_ok(x.shape[0], x.shape[1]):
+            return self._forward_fused(x)
         cfg, w = self.cfg, self.w
         B, S, d = x.shape
         D = cfg.head_dim

@@ -241,13 +241,14 @@ def _bf16(*ts):
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
-           heads_seq: int = 0) -> torch.Tensor:
+           heads_seq: int = 0, residual: torch.Tensor | None = None) -> torch.Tensor:
     """x @ weight.T on the tcgen05 GEMM (teeny-core Linear in the block).
 
     x: [..., k] row-major, or (heads_seq > 0) the attention output
     [B, H, heads_seq, 128], read as the [B * heads_seq, H * 128] matrix that
     merge_heads would build.  weight: [n, k].  Returns [..., n] (or
-    [B, heads_seq, n])."""
+    [B, heads_seq, n]); with ``residual`` (same shape as the output) returns
+    bf16(x @ weight.T) + residual."""
     _bf16(x, weight)
     n, k = weight.shape
     if heads_seq > 0:
@@ -262,8 +263,11 @@ def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = Non
     y = torch.empty(lead + (n,), dtype=x.dtype, device=x.device) if out is None else out
     _bf16(y)
     _need(y.numel() == m * n, "out has the wrong size")
-    call("tf_b200_gemm_bf16", _ptr(x), _ptr(weight), _ptr(y), m, n, k, int(heads_seq),
-         _stream(x))
+    if residual is not None:
+        _bf16(residual)
+        _need(residual.numel() == m * n, "residual has the wrong size")
+    call("tf_b200_gemm_bf16", _ptr(x), _ptr(weight), _ptr(residual), _ptr(y), m, n, k,
+         int(heads_seq), _stream(x))
     return y
 
 

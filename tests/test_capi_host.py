@@ -98,7 +98,7 @@ def test_rope_and_transpose_reject_bad_arguments(native_lib):
 
 
 def test_gemm_entries_reject_bad_arguments(native_lib):
-    g = lambda *a: _capi.raw("tf_b200_gemm_bf16", *a, None)
+    g = lambda a, b, c, *rest: _capi.raw("tf_b200_gemm_bf16", a, b, None, c, *rest, None)
     assert g(FAKE, FAKE, FAKE, -1, 256, 64, 0) == TF_ERR_INVALID_ARG
     assert g(FAKE, FAKE, FAKE, 0, 256, 64, 0) == TF_OK          # empty output: no-op
     assert g(FAKE, FAKE, FAKE, 128, 256, 0, 0) == TF_ERR_UNSUPPORTED

@@ -70,6 +70,30 @@ def _rank_main(rank, world, port, q):
         torch.cuda.synchronize()
         out["layer_err"] = float((y_peer.float() - y_nccl.float()).abs()
                                  .div(y_nccl.float().abs().clamp(min=1)).max())
+        # fused layer (QKV+RoPE epilogue, o_proj/down_proj pushing their row
+        # slices to the owner ranks, local-sum all-reduce) vs the separate-kernel
+        # layer with NCCL, and vs the fp32 reference of the whole layer
+        from llama_ref import layer_ref_fp32
+        cfg3 = LlamaLayerConfig(d_model=512, n_heads=4, n_kv_heads=2, head_dim=128, d_ff=1024)
+        full3 = init_full_weights(cfg3, seed=13, device=dev)
+        wsh3 = shard_weights(full3, cfg3, world, rank)
+        x3 = torch.randn((2, 128, 512), generator=torch.Generator(device=dev).manual_seed(6),
+                         device=dev).bfloat16()
+        ar3 = PeerAllReduceNorm(2 * 128, 512, device=dev)
+        fused = LlamaLayerTP(cfg3, wsh3, world=world, peer_ar=ar3)
+        assert fused.fused_ok(2, 128)
+        ys = [fused.forward(x3).clone() for _ in range(3)]  # repeated calls: epochs, reuse
+        y_ref3 = LlamaLayerTP(cfg3, wsh3, world=world, fused=False,
+                              all_reduce=lambda t: dist.all_reduce(t)).forward(x3)
+        torch.cuda.synchronize()
+        out["fused_err"] = float((ys[-1].float() - y_ref3.float()).abs()
+                                 .div(y_ref3.float().abs().clamp(min=1)).max())
+        out["fused_repeat"] = all(torch.equal(ys[0], y) for y in ys[1:])
+        if rank == 0:
+            ref = layer_ref_fp32(x3.float().cpu(), full3, cfg3, 4, 2)
+            out["fused_ref_err"] = float((ys[-1].float().cpu() - ref).abs()
+                                         .div(ref.abs().clamp(min=1)).max())
+        out["status2"] = tfb.device_status(clear=True)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -104,3 +128,7 @@ def test_peer_allreduce_residual_rmsnorm_2gpu():
         # h: fp32 sum rounded once to bf16 (2^-9 relative); y from that h
         assert rel_h <= 1e-2 and rel_y <= 2e-2, out["ar_errs"]
     assert out["layer_err"] <= 3e-2, out["layer_err"]
+    assert out["status2"] == 0
+    assert out["fused_err"] <= 3e-2, out["fused_err"]
+    assert out["fused_ref_err"] <= 3e-2, out["fused_ref_err"]
+    assert out["fused_repeat"], "fused TP layer must be repeatable"
