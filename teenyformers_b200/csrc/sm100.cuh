@@ -4,8 +4,9 @@
 // with shared-memory matrix descriptors.
 //
 // Descriptor encodings follow the PTX ISA (tcgen05 "shared memory descriptor"
-// and "instruction descriptor" tables).  Only single-CTA (cta_group::1)
-// forms are used and no load uses cluster multicast.
+// and "instruction descriptor" tables).  The forms here are single-CTA
+// (cta_group::1); the GEMM's CTA-pair (cta_group::2) forms are in
+// gemm_sm100.cuh.  No load anywhere uses cluster multicast.
 #pragma once
 
 #include <cuda.h>

@@ -111,6 +111,7 @@ int current_device() {
 }
 
 int g_num_sms[kMaxDevices];
+int g_pair_clusters[kMaxDevices];
 
 // Raises the dynamic shared-memory limit of every kernel that needs more
 // than 48 KB and records the SM count, once per device.
@@ -135,10 +136,25 @@ int ensure_device_setup() {
     set((const void*)fa_bwd_fused_sm100_kernel<128>, BwdFusedCfg<128>::SMEM_BYTES);
     set((const void*)fa_decode_kernel<64>, DecCfg<64>::SMEM_BYTES);
     set((const void*)fa_decode_kernel<128>, DecCfg<128>::SMEM_BYTES);
-    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_STORE>, GemmCfg::SMEM_ALLOC);
-    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_SWIGLU>, GemmCfg::SMEM_ALLOC);
-    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_QKV_ROPE>, GemmCfg::SMEM_ALLOC);
-    set((const void*)gemm_bf16_sm100_kernel<GEMM_EPI_PUSH>, GemmCfg::SMEM_ALLOC);
+    set((const void*)gemm_bf16_sm100_pair_kernel<GEMM_EPI_STORE>, GemmPairCfg::SMEM_ALLOC);
+    set((const void*)gemm_bf16_sm100_pair_kernel<GEMM_EPI_SWIGLU>, GemmPairCfg::SMEM_ALLOC);
+    set((const void*)gemm_bf16_sm100_pair_kernel<GEMM_EPI_QKV_ROPE>, GemmPairCfg::SMEM_ALLOC);
+    set((const void*)gemm_bf16_sm100_pair_kernel<GEMM_EPI_PUSH>, GemmPairCfg::SMEM_ALLOC);
+    // CTA pairs that fit at once (SMs pair up within a GPC; one CTA per SM)
+    g_pair_clusters[dev] = g_num_sms[dev] / 2;
+    if (e == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, 1, 1);
+      cfg.blockDim = dim3(kGemmThreads, 1, 1);
+      cfg.dynamicSmemBytes = GemmPairCfg::SMEM_ALLOC;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(
+              &n, (const void*)gemm_bf16_sm100_pair_kernel<GEMM_EPI_STORE>, &cfg) == cudaSuccess &&
+          n > 0)
+        g_pair_clusters[dev] = n;
+      else
+        (void)cudaGetLastError();
+    }
     const int f32_max = (3 * kF32Rows + 3 * kF32Tile) * kF32MaxD * 4 + 2 * kF32Tile * 4;
     set((const void*)fa_fwd_f32_kernel, f32_max);
     set((const void*)fa_bwd_dq_f32_kernel, f32_max);
@@ -714,7 +730,7 @@ extern "C" int tf_b200_swiglu_bf16(const void* z, void* out, int rows, int d_ff,
 // ===================================================================== GEMMs with fused epilogues
 namespace {
 
-// Shared validation + launch of gemm_bf16_sm100_kernel.  A is row-major
+// Shared validation + launch of gemm_bf16_sm100_pair_kernel.  A is row-major
 // [m, k], or (a_seq > 0) the attention output [m / a_seq, k / 128, a_seq, 128].
 template <int EPI>
 int gemm_launch(const void* a, const void* b, int m, int n, int k, int a_seq, GemmParams& prm,
@@ -735,20 +751,22 @@ int gemm_launch(const void* a, const void* b, int m, int n, int k, int a_seq, Ge
   } else {
     ok = make_bf16_2d_map(&ta, a, k, m, kGemmBM);
   }
-  if (!ok || !make_bf16_2d_map(&tb, b, k, n, kGemmBN)) return TF_ERR_CUDA;
+  // CTA pairs: 256 x 256 tiles, each CTA loads 128 rows of A and of B
+  if (!ok || !make_bf16_2d_map(&tb, b, k, n, 128)) return TF_ERR_CUDA;
   prm.M = m, prm.N = n, prm.K = k;
-  prm.n_mblk = (m + kGemmBM - 1) / kGemmBM;
+  prm.n_mblk = (m + 255) / 256;
   prm.n_nblk = (n + kGemmBN - 1) / kGemmBN;
   prm.n_kblk = (k + kGemmBK - 1) / kGemmBK;
   const long long tiles = (long long)prm.n_mblk * prm.n_nblk;
   if (!fits_i32(tiles)) return TF_ERR_TOO_LARGE;
   prm.n_tiles = (int)tiles;
-  prm.group_m = std::min(prm.n_mblk, 16);
+  prm.group_m = std::min(prm.n_mblk, 8);
   prm.a_heads = a_seq > 0 ? 1 : 0;
   prm.a_seq = a_seq > 0 ? a_seq : 1;
   prm.a_n_heads = a_seq > 0 ? k / kGemmHeadDim : 0;
-  gemm_bf16_sm100_kernel<EPI>
-      <<<persistent_grid(tiles), kGemmThreads, GemmCfg::SMEM_ALLOC, st>>>(ta, tb, prm);
+  const long long clusters = std::min<long long>(tiles, g_pair_clusters[current_device()]);
+  gemm_bf16_sm100_pair_kernel<EPI>
+      <<<(unsigned)(2 * clusters), kGemmThreads, GemmPairCfg::SMEM_ALLOC, st>>>(ta, tb, prm);
   return launch_status();
 }
 
