@@ -326,25 +326,32 @@ def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
     flops = cfg.flops(tokens, c["seq"])
     n = max(3, min(args.steps, 10))
 
-    def measure(layer):
-        for _ in range(args.warmup):
-            layer.forward(x)
+    def measure_interleaved(layers, rounds=3):
+        """Median over `rounds` of each layer's mean step time; the variants
+        alternate within every round so they see the same clock / power state
+        (the GPU runs at its power cap here and its clocks drift over seconds)."""
+        for layer in layers:
+            for _ in range(args.warmup):
+                layer.forward(x)
+        times = [[] for _ in layers]
+        for _ in range(rounds):
+            for i, layer in enumerate(layers):
+                barrier()
+                torch.cuda.synchronize()
+                times[i].append(max_over_ranks(_timed(stream, n, lambda: layer.forward(x))))
         barrier()
-        torch.cuda.synchronize()
-        ms = max_over_ranks(_timed(stream, n, lambda: layer.forward(x)))
-        barrier()
-        return ms
+        return [sorted(t)[len(t) // 2] for t in times]
 
     res = {}
     if world > 1:
         from teenyformers_b200.tp import PeerAllReduceNorm
         peer = PeerAllReduceNorm(tokens, c["d_model"], device=dev)
-        ms_nccl = measure(LlamaLayerTP(cfg, w, world=world, fused=False,
-                                       all_reduce=lambda t: dist.all_reduce(t)))
-        ms_peer = measure(LlamaLayerTP(cfg, w, world=world, peer_ar=peer, fused=False))
         layer = LlamaLayerTP(cfg, w, world=world, peer_ar=peer)
         assert layer.fused_ok(c["batch"], c["seq"])
-        ms = measure(layer)
+        ms, ms_peer, ms_nccl = measure_interleaved([
+            layer, LlamaLayerTP(cfg, w, world=world, peer_ar=peer, fused=False),
+            LlamaLayerTP(cfg, w, world=world, fused=False,
+                         all_reduce=lambda t: dist.all_reduce(t))])
         res["nccl_allreduce_ms_per_step"] = ms_nccl
         res["nccl_allreduce_tflops"] = flops / (ms_nccl * 1e-3) / 1e12
         res["unfused_peer_ms_per_step"] = ms_peer
@@ -355,10 +362,10 @@ def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
                       "unfused_peer_* = the same with the peer all-reduce kernel")
         launches = 8
     else:
-        ms_unfused = measure(LlamaLayerTP(cfg, w, world=world, fused=False))
         layer = LlamaLayerTP(cfg, w, world=world)
         assert layer.fused_ok(c["batch"], c["seq"])
-        ms = measure(layer)
+        ms, ms_unfused = measure_interleaved([layer, LlamaLayerTP(cfg, w, world=world,
+                                                                  fused=False)])
         res["unfused_ms_per_step"] = ms_unfused
         res["unfused_tflops"] = flops / (ms_unfused * 1e-3) / 1e12
         collective = ("no collective at TP x1; unfused_* = cuBLAS projections + separate "
@@ -368,7 +375,8 @@ def llama_leg(args, dev, world, rank, barrier, max_over_ranks, peaks):
     del w, x, layer
     res["device_status"] = tfb_status()
     res.update({"tflops": tf, "tokens_per_s": tokens / (ms * 1e-3), "ms_per_step": ms,
-                "steps": n, "flops_per_step": flops,
+                "steps": n, "timing": "median of 3 rounds, variants interleaved within a round",
+                "flops_per_step": flops,
                 "frac_of_peak": tf / world / peaks["bf16_tflops_sustained"],
                 "launches_per_step_ours": launches,
                 "workload": f"config#5 Llama-3-8B-shaped layer prefill B{c['batch']} S{c['seq']} "
