@@ -639,6 +639,13 @@ def main():
 
     if rank == 0:
         traffic = load_traffic()
+        # the committed traffic is for config #3's 256 heads on one GPU; a rank's share
+        # (or the --small case) moves bytes in proportion to its heads
+        t_scale = bh_local / 256.0
+
+        def t_of(key):
+            v = traffic.get(key)
+            return None if v is None else v * t_scale
         bf16_peak = peaks["bf16_tflops_sustained"]
         fwd_ach = fwd_tflops_rank
         bwd_ach = bwd_tflops_rank
@@ -646,13 +653,13 @@ def main():
         roof_fwd = {"kernel": "fa_fwd_sm100_kernel<128>", "bound": "tensor", "achieved": fwd_ach,
                     "peak": bf16_peak, "unit": "TFLOP/s", "frac": fwd_ach / bf16_peak,
                     "frac_of_burst": fwd_ach / peaks["bf16_tflops"],
-                    "traffic": traffic.get("fa_fwd"),
+                    "traffic": t_of("fa_fwd"),
                     "flops_per_launch": fwd_flops_rank, "ms_per_launch": fwd_ms}
         roof_bwd = {"kernel": "fa_bwd (prep + fused dK/dV/dQ + dQ convert kernels, one C-ABI call)",
                     "bound": "tensor", "achieved": bwd_ach, "peak": bf16_peak,
                     "unit": "TFLOP/s", "frac": bwd_ach / bf16_peak,
                     "frac_of_burst": bwd_ach / peaks["bf16_tflops"],
-                    "traffic": traffic.get("fa_bwd"),
+                    "traffic": t_of("fa_bwd"),
                     "flops_per_launch": bwd_flops_rank, "ms_per_launch": bwd_ms}
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
