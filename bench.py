@@ -544,12 +544,14 @@ def main():
                             f"{n_rope} launches in one CUDA graph replay"}
         del xs, ys
 
+    # the memory-bound decode leg goes before the long tensor-bound legs, which leave the
+    # GPU at its power cap with lowered SM clocks
+    decode = None if args.no_decode else decode_leg(args, dev, world, rank, barrier,
+                                                    max_over_ranks, peaks)
     gqa = None if args.no_gqa else gqa_leg(args, dev, world, rank, barrier, max_over_ranks,
                                            peaks)
     llama = None if args.no_llama else llama_leg(args, dev, world, rank, barrier,
                                                  max_over_ranks, peaks)
-    decode = None if args.no_decode else decode_leg(args, dev, world, rank, barrier,
-                                                    max_over_ranks, peaks)
 
     clocks = sampler.stop() if rank == 0 else None
 
