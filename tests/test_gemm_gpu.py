@@ -130,12 +130,13 @@ def test_rope_table_matches_rope_kernel_angles(cuda_device):
     np.testing.assert_array_equal(rot[:, 1::2], t[:, :, 1])
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("heads", [False, True])
-def test_linear_push_places_rows_by_owner(cuda_device, heads):
-    """Two emulated ranks push their partial products; receive buffer o then holds
+def test_linear_push_places_rows_by_owner(cuda_device, heads, world):
+    """`world` emulated ranks push their partial products; receive buffer o then holds
     rank r's rows [o*slice, (o+1)*slice) at slot r, bit-equal to the plain GEMM."""
     import teenyformers_b200 as tfb
-    world, B, S, H, n = 2, 2, 256, 4, 512
+    B, S, H, n = 2, 128 * world, 4, 512
     m, k = B * S, H * 128
     slice_rows = m // world
     recv = [torch.full((world, slice_rows, n), float("nan"), dtype=torch.bfloat16,
