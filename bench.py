@@ -457,6 +457,7 @@ def main():
     lse = torch.empty((1, bh_local, S), device=dev, dtype=torch.float32)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     ws = tfb.bwd_workspace(q)
+    step_bytes = 8 * q.numel() * 2 + ws.numel()  # the tensors one step touches, + workspace
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -680,8 +681,11 @@ def main():
                                    + (" (small profiling case)" if args.small else ""),
                        "batch": B, "heads": H, "seq_len": S, "head_dim": D,
                        "heads_per_gpu": bh_local, "parallelism": f"bh-shard x{world}",
-                       "l2": "inputs larger than L2 (each of Q,K,V,dO is "
-                             f"{q.numel() * 2 / 2**20:.0f} MiB per GPU)"},
+                       "l2": "inputs larger than L2: each step reads and writes "
+                             f"{step_bytes / 2**20:.0f} MiB per GPU (Q,K,V,dO,O,dQ,dK,dV of "
+                             f"{q.numel() * 2 / 2**20:.0f} MiB each + the fp32 dQ accumulator) "
+                             "against a 126 MB L2, so each step starts with the previous "
+                             "step's inputs evicted"},
             "fwd_tflops": fwd_flops_total / (fwd_ms * 1e-3) / 1e12,
             "bwd_tflops": bwd_flops_total / (bwd_ms * 1e-3) / 1e12,
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
