@@ -88,6 +88,11 @@ struct GemmParams {
   // PUSH: receive buffer of every rank ([world, slice_rows, N] each)
   __nv_bfloat16* peer_out[kGemmMaxPeers];
   int rank, world, slice_rows;
+  // the walk over tiles starts at tile tile_rotate (0 <= tile_rotate < n_tiles)
+  // and wraps: PUSH gives each rank a different starting owner so the ranks'
+  // peer stores spread over every NVLink destination instead of all ranks
+  // writing into one owner at a time
+  int tile_rotate;
 };
 
 __device__ __forceinline__ void gemm_sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
@@ -109,6 +114,8 @@ __device__ __forceinline__ uint4 gemm_lds128(uint32_t addr) {
 // column blocks, row block fastest, so the CTAs running at once share a few
 // column blocks of B and a few row blocks of A in L2.
 __device__ __forceinline__ void gemm_tile(const GemmParams& p, int t, int& mb, int& nb) {
+  t += p.tile_rotate;
+  if (t >= p.n_tiles) t -= p.n_tiles;
   const int per_group = p.group_m * p.n_nblk;
   const int g = t / per_group;
   const int m_first = g * p.group_m;

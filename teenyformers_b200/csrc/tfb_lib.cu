@@ -761,6 +761,11 @@ int gemm_launch(const void* a, const void* b, int m, int n, int k, int a_seq, Ge
   if (!fits_i32(tiles)) return TF_ERR_TOO_LARGE;
   prm.n_tiles = (int)tiles;
   prm.group_m = std::min(prm.n_mblk, 8);
+  // PUSH: rank r's walk starts with the rows of owner (r + 1) % world (each owner's
+  // rows are a contiguous run of row blocks, so of tiles) and ends with its own
+  prm.tile_rotate = 0;
+  if (EPI == GEMM_EPI_PUSH && prm.world > 1)
+    prm.tile_rotate = (int)(((long long)((prm.rank + 1) % prm.world) * tiles / prm.world) % tiles);
   prm.a_heads = a_seq > 0 ? 1 : 0;
   prm.a_seq = a_seq > 0 ? a_seq : 1;
   prm.a_n_heads = a_seq > 0 ? k / kGemmHeadDim : 0;
