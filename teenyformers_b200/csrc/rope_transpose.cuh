@@ -14,8 +14,9 @@
 //
 // HBM-bound: every element is read once and written once with 16-byte
 // vector accesses; each row is a contiguous D*elem-byte run on both sides.
-// One CTA handles one position s for a block of (b, h) rows so that sin/cos
-// of that position are computed once per thread and reused across rows.
+// One CTA handles one position s for a block of (b, h) rows: the position's
+// D/2 (cos, sin) pairs are computed once into shared memory and reused across
+// the rows.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -63,6 +64,8 @@ __device__ __forceinline__ size_t row_offset(int layout, int b, int s, int h, in
   return layout == LAYOUT_BSHD ? ((size_t)b * S + s) * H + h : ((size_t)b * H + h) * S + s;
 }
 
+constexpr int kRopeMaxHalf = 1024;  // D <= 2048
+
 // grid = (S, ceil(B*H / rows_per_cta)), block = 256.
 // STYLE 0: interleaved pairs; 1: rotate-half.  INV: inverse rotation.
 template <typename T, int STYLE, bool INV>
@@ -76,22 +79,28 @@ __global__ void __launch_bounds__(256)
   const int rows_per_pass = blockDim.x / cpr;
   const int c = threadIdx.x % cpr;
   const int r0 = threadIdx.x / cpr;
-  if (r0 >= rows_per_pass) return;
   const int row_lo = blockIdx.y * rows_per_cta;
   const int row_hi = min(B * H, row_lo + rows_per_cta);
 
-  // Angles for the pairs this thread owns (computed once, reused over rows).
-  constexpr int NP = STYLE == 0 ? EPV / 2 : EPV;
-  float cs[NP], sn[NP];
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const int k = STYLE == 0 ? c * (EPV / 2) + i : c * EPV + i;
+  // The D/2 angles of this position, computed once per CTA (each pair by one
+  // thread) and shared: a thread then reads the pairs it owns.
+  __shared__ float2 ang[kRopeMaxHalf];
+  for (int k = threadIdx.x; k < D / 2; k += blockDim.x) {
     const float inv_freq = expf((float)k * coef);
     const float theta = (float)s * inv_freq;
     float sv, cv;
     sincosf(theta, &sv, &cv);
-    cs[i] = cv;
-    sn[i] = INV ? -sv : sv;
+    ang[k] = make_float2(cv, INV ? -sv : sv);
+  }
+  __syncthreads();
+  if (r0 >= rows_per_pass) return;
+  constexpr int NP = STYLE == 0 ? EPV / 2 : EPV;
+  float cs[NP], sn[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const float2 a = ang[STYLE == 0 ? c * (EPV / 2) + i : c * EPV + i];
+    cs[i] = a.x;
+    sn[i] = a.y;
   }
 
   const size_t row_elems = (size_t)D;
