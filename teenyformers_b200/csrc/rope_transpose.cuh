@@ -82,6 +82,27 @@ __global__ void __launch_bounds__(256)
   const int row_lo = blockIdx.y * rows_per_cta;
   const int row_hi = min(B * H, row_lo + rows_per_cta);
 
+  const size_t row_elems = (size_t)D;
+  const int half_vecs = D / (2 * EPV);
+  auto src_of = [&](int r) {
+    const int b = r / H, h = r % H;
+    return reinterpret_cast<const uint4*>(x + row_offset(in_layout, b, s, h, S, H) * row_elems);
+  };
+  // The first kPre rows' loads go out before the angles are computed, so the
+  // memory system is busy while the CTA evaluates them.
+  constexpr int kPre = 4;
+  const bool active = r0 < rows_per_pass;
+  uint4 pre0[kPre], pre1[kPre];
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int r = row_lo + r0 + j * rows_per_pass;
+    if (active && r < row_hi) {
+      const uint4* sp = src_of(r);
+      pre0[j] = __ldcs(sp + c);
+      pre1[j] = STYLE == 1 ? __ldcs(sp + c + half_vecs) : pre0[j];
+    }
+  }
+
   // The D/2 angles of this position, computed once per CTA (each pair by one
   // thread) and shared: a thread then reads the pairs it owns.
   __shared__ float2 ang[kRopeMaxHalf];
@@ -93,7 +114,7 @@ __global__ void __launch_bounds__(256)
     ang[k] = make_float2(cv, INV ? -sv : sv);
   }
   __syncthreads();
-  if (r0 >= rows_per_pass) return;
+  if (!active) return;
   constexpr int NP = STYLE == 0 ? EPV / 2 : EPV;
   float cs[NP], sn[NP];
 #pragma unroll
@@ -103,27 +124,21 @@ __global__ void __launch_bounds__(256)
     sn[i] = a.y;
   }
 
-  const size_t row_elems = (size_t)D;
-#pragma unroll 4
-  for (int r = row_lo + r0; r < row_hi; r += rows_per_pass) {
+  // rotates row r's vector(s) v0 (and v1 for rotate-half) and stores them
+  auto rotate_store = [&](int r, const uint4& v0, const uint4& v1) {
     const int b = r / H, h = r % H;
-    const T* src = x + row_offset(in_layout, b, s, h, S, H) * row_elems;
-    T* dst = y + row_offset(out_layout, b, s, h, S, H) * row_elems;
+    uint4* dst = reinterpret_cast<uint4*>(y + row_offset(out_layout, b, s, h, S, H) * row_elems);
     if (STYLE == 0) {
-      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src) + c);
       float f[EPV];
-      unpack16(v, f, T());
+      unpack16(v0, f, T());
 #pragma unroll
       for (int i = 0; i < EPV / 2; ++i) {
         const float a = f[2 * i], bb = f[2 * i + 1];
         f[2 * i] = a * cs[i] - bb * sn[i];
         f[2 * i + 1] = a * sn[i] + bb * cs[i];
       }
-      __stcs(reinterpret_cast<uint4*>(dst) + c, pack16(f, T()));
+      __stcs(dst + c, pack16(f, T()));
     } else {
-      const int half_vecs = D / (2 * EPV);
-      const uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(src) + c);
-      const uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(src) + c + half_vecs);
       float f0[EPV], f1[EPV];
       unpack16(v0, f0, T());
       unpack16(v1, f1, T());
@@ -133,9 +148,21 @@ __global__ void __launch_bounds__(256)
         f0[i] = a * cs[i] - bb * sn[i];
         f1[i] = a * sn[i] + bb * cs[i];
       }
-      __stcs(reinterpret_cast<uint4*>(dst) + c, pack16(f0, T()));
-      __stcs(reinterpret_cast<uint4*>(dst) + c + half_vecs, pack16(f1, T()));
+      __stcs(dst + c, pack16(f0, T()));
+      __stcs(dst + c + half_vecs, pack16(f1, T()));
     }
+  };
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int r = row_lo + r0 + j * rows_per_pass;
+    if (r < row_hi) rotate_store(r, pre0[j], pre1[j]);
+  }
+#pragma unroll 8
+  for (int r = row_lo + r0 + kPre * rows_per_pass; r < row_hi; r += rows_per_pass) {
+    const uint4* sp = src_of(r);
+    const uint4 v0 = __ldcs(sp + c);
+    const uint4 v1 = STYLE == 1 ? __ldcs(sp + c + half_vecs) : v0;
+    rotate_store(r, v0, v1);
   }
 }
 
@@ -156,8 +183,32 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Pure copy between [B,S,H,D] and [B,H,S,D] (either direction) for rows of
+// whole 16-byte vectors (vpr per row): laid out like rope_rows_kernel -- one
+// CTA per position s covers its (b, h) rows (split over blockIdx.y when S is
+// small), a thread copies one vector column of a row per pass, streaming
+// loads and stores.  Bit-exact.
+__global__ void __launch_bounds__(256)
+    transpose_rows16_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, int B, int S,
+                            int H, int vpr, int in_layout, int out_layout, int rows_per_cta) {
+  const int s = blockIdx.x;
+  const int rows_per_pass = blockDim.x / vpr;
+  const int c = threadIdx.x % vpr;
+  const int r0 = threadIdx.x / vpr;
+  if (r0 >= rows_per_pass) return;
+  const int row_lo = blockIdx.y * rows_per_cta;
+  const int row_hi = min(B * H, row_lo + rows_per_cta);
+#pragma unroll 8
+  for (int r = row_lo + r0; r < row_hi; r += rows_per_pass) {
+    const int b = r / H, h = r % H;
+    const uint4 v = __ldcs(x + row_offset(in_layout, b, s, h, S, H) * vpr + c);
+    __stcs(y + row_offset(out_layout, b, s, h, S, H) * vpr + c, v);
+  }
+}
+
 // Pure copy between [B,S,H,D] and [B,H,S,D] (either direction), any element
-// size: bit-exact.  VEC = bytes moved per access (16, 8, 4, 2 or 1).
+// size: bit-exact.  VEC = bytes moved per access (16, 8, 4, 2 or 1).  Used
+// when rows are not whole 16-byte vectors or pointers are not 16-byte aligned.
 template <typename V>
 __global__ void __launch_bounds__(256)
     transpose_rows_kernel(const V* __restrict__ x, V* __restrict__ y, int B, int S, int H,

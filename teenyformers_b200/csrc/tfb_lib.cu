@@ -582,6 +582,23 @@ int launch_transpose(const void* src, void* dst, int B, int S, int H, int D, int
   const long long total = (long long)B * S * H * vpr;
   if (!fits_i32(vpr) || !fits_i32((long long)B * S) || !fits_i32((long long)B * H))
     return TF_ERR_TOO_LARGE;
+  if (vec == 16 && vpr <= 256 && S <= 0x7fffffff) {
+    // whole 16-byte vectors: row-wise kernel, one CTA per position (sized as
+    // for RoPE: the rows of a position split only when positions are few)
+    const long long rows = (long long)B * H;
+    const int rows_per_pass = (int)(256 / vpr);
+    const long long target = 148LL * 8;
+    long long per_cta = rows;
+    if (S < target) per_cta = (rows + (target + S - 1) / S - 1) / ((target + S - 1) / S);
+    per_cta = ((per_cta + rows_per_pass - 1) / rows_per_pass) * rows_per_pass;
+    const long long gy = (rows + per_cta - 1) / per_cta;
+    if (gy <= 65535) {
+      transpose_rows16_kernel<<<dim3((unsigned)S, (unsigned)gy), 256, 0, st>>>(
+          static_cast<const uint4*>(src), static_cast<uint4*>(dst), B, S, H, (int)vpr,
+          in_layout, out_layout, (int)per_cta);
+      return launch_status();
+    }
+  }
   const long long blocks_needed = (total + 255) / 256;
   const unsigned blocks = (unsigned)(blocks_needed < 148LL * 32 ? blocks_needed : 148LL * 32);
 #define TFB_TR(VT)                                                                       \
