@@ -89,8 +89,9 @@ __global__ void __launch_bounds__(256)
     return reinterpret_cast<const uint4*>(x + row_offset(in_layout, b, s, h, S, H) * row_elems);
   };
   // The first kPre rows' loads go out before the angles are computed, so the
-  // memory system is busy while the CTA evaluates them.
-  constexpr int kPre = 4;
+  // memory system is busy while the CTA evaluates them (8 single vectors for
+  // interleaved pairs, 4 vector pairs for rotate-half).
+  constexpr int kPre = STYLE == 0 ? 8 : 4;
   const bool active = r0 < rows_per_pass;
   uint4 pre0[kPre], pre1[kPre];
 #pragma unroll
