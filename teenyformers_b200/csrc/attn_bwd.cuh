@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(bar(KB_QFULL + s), 1);
       mbar_init(bar(KB_QEMPTY + s), 1);
       mbar_init(bar(KB_SFULL + s), 1);
-      mbar_init(bar(KB_PFULL + s), 256);
+      mbar_init(bar(KB_PFULL + s), 8);  // one arrival per elementwise warp
     }
     mbar_init(bar(KB_ACC), 1);
     mbar_init(bar(KB_DRAIN), 1);
@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(KB_PFULL + h));
+      mbar_arrive_warp(bar(KB_PFULL + h));
     }
     // ---- epilogue: warpgroups 0,1 write dV, 2,3 dK (= acc * scale), 64 columns each
     const bool valid = key < p.Sk;
@@ -546,16 +546,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int n_items = p.BHq * p.n_qt;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(QB_Q), 512);
+    mbar_init(bar(QB_Q), 16);  // one arrival per elementwise warp
     mbar_init(bar(QB_QFREE), 1);
-    mbar_init(bar(QB_DQFREE), 512);
+    mbar_init(bar(QB_DQFREE), 16);
     for (int s = 0; s < C::KV_STAGES; ++s) {
       mbar_init(bar(QB_KVFULL + s), 1);
       mbar_init(bar(QB_KVEMPTY + s), 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(QB_SFULL + s), 1);
-      mbar_init(bar(QB_PFULL + s), 256);
+      mbar_init(bar(QB_PFULL + s), 8);
     }
     mbar_init(bar(QB_ACC), 1);
     mbar_init(bar(QB_DRAIN), 1);
@@ -754,7 +754,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(bar(QB_DQFREE));
+      mbar_arrive_warp(bar(QB_DQFREE));
       return true;
     };
     for (; ok; ++li) {
@@ -776,7 +776,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(QB_Q));
+      mbar_arrive_warp(bar(QB_Q));
       const float nlse2 = pre_nlse2, ndelta = pre_ndelta;
       if (sched_item(li + 1) < n_items) prefetch(sched_item(li + 1));
       // the previous item's dQ, overlapping this item's first S MMAs
@@ -826,7 +826,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(QB_PFULL + h));
+        mbar_arrive_warp(bar(QB_PFULL + h));
       }
       g += it.n_kv;
       prev_w = w;

@@ -194,13 +194,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     mbar_init(bar(FB2_DOFULL), 1);
     mbar_init(bar(FB2_DOEMPTY), 1);
     mbar_init(bar(FB2_SFULL), 1);
-    mbar_init(bar(FB2_PFULL), 256);
+    mbar_init(bar(FB2_PFULL), 8);  // one arrival per elementwise warp
     mbar_init(bar(FB2_DPFULL), 1);
-    mbar_init(bar(FB2_DSFULL), 256);
+    mbar_init(bar(FB2_DSFULL), 8);
     mbar_init(bar(FB2_DQFULL), 1);
-    mbar_init(bar(FB2_DQEMPTY), 128);
+    mbar_init(bar(FB2_DQEMPTY), 4);  // one per reduction warp
     mbar_init(bar(FB2_ACC), 1);
-    mbar_init(bar(FB2_ACCFREE), 256);
+    mbar_init(bar(FB2_ACCFREE), 8);
     for (int s = 0; s < kItemRing; ++s) {
       mbar_init(bar(FB2_ITEMFULL + s), 1);
       mbar_init(bar(FB2_ITEMEMPTY + s), kItemConsumers);
@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(FB2_PFULL));
+        mbar_arrive_warp(bar(FB2_PFULL));
         // Phase 2: dS^T = P^T (dP^T - D): bf16 packed over dP^T (A of dK) and
         // into the shared dS tile (A of dQ).
         ok = __all_sync(0xffffffffu, mbar_wait(bar(FB2_DPFULL), g & 1, abort_flag, 633));
@@ -541,7 +541,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         tmem_wait_st();
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(bar(FB2_DSFULL));
+        mbar_arrive_warp(bar(FB2_DSFULL));
       }
       if (!ok) break;
       // ---- epilogue: warpgroup 0 writes dV, 1 writes dK (= acc * scale); the
@@ -558,7 +558,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         tmem_wait_ld();
         if (c == D / 32 - 1) {
           tc_fence_before();
-          mbar_arrive(bar(FB2_ACCFREE));
+          mbar_arrive_warp(bar(FB2_ACCFREE));
         }
         if (valid) store_row_chunk_bf16(out_row + c * 32, r, mul);
       }
@@ -593,7 +593,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                     *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(bar(FB2_DQEMPTY));
+        mbar_arrive_warp(bar(FB2_DQEMPTY));
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           // chunk c of every tile uses buffer c & 1 (D / 32 chunks per tile is even)

@@ -160,10 +160,10 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(FB_VFULL + s), 1);
       mbar_init(bar(FB_VEMPTY + s), 1);
       mbar_init(bar(FB_SFULL + s), 1);
-      mbar_init(bar(FB_PFULL + s), 128);
-      mbar_init(bar(FB_PFULL1 + s), 128);
+      mbar_init(bar(FB_PFULL + s), 4);  // one arrival per softmax warp
+      mbar_init(bar(FB_PFULL1 + s), 4);
       mbar_init(bar(FB_ODONE + s), 1);
-      mbar_init(bar(FB_OFREE + s), 128);
+      mbar_init(bar(FB_OFREE + s), 4);
     }
     mbar_init(bar(FB_DRAIN), 1);
     *abort_flag = 0;
@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(320, 1)
           }
           tmem_wait_st();
           tc_fence_before();
-          mbar_arrive(bar((half == 0 ? FB_PFULL : FB_PFULL1) + t));
+          mbar_arrive_warp(bar((half == 0 ? FB_PFULL : FB_PFULL1) + t));
         }
         float a0, a1, a2, a3;
         f2_split(acc2[0], a0, a1);
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(320, 1)
         tmem_wait_ld();
         if (c == D / 32 - 1) {
           tc_fence_before();
-          mbar_arrive(bar(FB_OFREE + t));
+          mbar_arrive_warp(bar(FB_OFREE + t));
         }
         uint32_t w[16];
 #pragma unroll

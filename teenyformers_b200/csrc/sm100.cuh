@@ -50,6 +50,17 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// One arrival per warp, for barriers whose count is the number of arriving
+// warps.  Each lane has already fenced its own writes (tcgen05.wait::st +
+// tcgen05.fence::before_thread_sync for TMEM, fence.proxy.async for shared
+// memory read by TMA / MMA); __syncwarp orders every lane's writes before
+// lane 0's release-arrive.  Thirty-two lanes arriving on one mbarrier are 32
+// serialised same-address shared-memory atomics; one arrival is one.
+__device__ __forceinline__ void mbar_arrive_warp(uint32_t bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
                "r"(bytes)
