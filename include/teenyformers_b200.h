@@ -100,15 +100,15 @@ TF_API int tf_b200_flash_attn2_bwd_bf16(const void* q, const void* k, const void
 /* Backward without caller-provided scratch.  No counterpart in the reference.
  * For callers that cannot allocate device memory at the point of the call:
  * an executor that plans every buffer up front from the ops' declared
- * shapes -- as teenyformers' does, handing a backward exactly q, k, v, o,
- * dO, l, dq, dk, dv (src/kernels/flash_attn2.rs:492-519) with no slot for
- * extra scratch -- or a process that forbids allocation once it is running.
+ * shapes and hands a backward only its tensors, with no slot for extra
+ * scratch, or a process that forbids allocation once it is running.
  * The per-row softmax statistics live instead in a fixed 8 MiB array inside
  * the library (held on every GPU that loads it, until exit), so
  * batch * n_heads_q * round_up(n_ctx_q, 128) must be <= 1,048,576
  * (e.g. B*H = 256 at S = 4096); larger problems return TF_ERR_TOO_LARGE.
  * The first call on a device looks the array up (cudaGetSymbolAddress) with
- * that device current; make that first call before any stream capture.
+ * that device current; make that first call before any stream capture.  A
+ * lookup that fails returns TF_ERR_CUDA and is tried again by the next call.
  * Nothing here calls cudaMalloc/cudaFree.  Every call shares the one array,
  * so calls that can overlap on the GPU (different streams) race: serialise
  * them.  Same arguments and results as tf_b200_flash_attn2_bwd_bf16 minus

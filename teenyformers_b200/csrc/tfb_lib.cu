@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/teenyformers_b200.h"
@@ -259,7 +260,10 @@ extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const 
 extern "C" size_t tf_b200_flash_attn2_bwd_workspace_size(int batch, int n_heads_q,
                                                          int n_ctx_q) {
   if (batch <= 0 || n_heads_q <= 0 || n_ctx_q <= 0) return 0;
-  return bwd_fused_workspace_bytes((long long)batch * n_heads_q, n_ctx_q);
+  // sizes the backward itself rejects as too large get 0 (and no overflow)
+  const long long bhq = (long long)batch * n_heads_q;
+  if (!fits_i32(bhq) || !fits_i32(bhq * ((n_ctx_q + 127) / 128))) return 0;
+  return bwd_fused_workspace_bytes(bhq, n_ctx_q);
 }
 
 namespace {
@@ -286,6 +290,8 @@ int bwd_bf16_impl(const void* q, const void* k, const void* v, const void* o, co
   if (!(softmax_scale > 0.0f) || !std::isfinite(softmax_scale)) return TF_ERR_INVALID_ARG;
   const long long bhq = (long long)batch * n_heads_q;
   const long long bhkv = (long long)batch * n_heads_kv;
+  // head counts first, so the products below stay far inside 64 bits
+  if (!fits_i32(bhq) || !fits_i32(bhkv)) return TF_ERR_TOO_LARGE;
   if (!fits_i32(bhq * ((n_ctx_q + 127) / 128)) || !fits_i32(bhkv * ((n_ctx_k + 127) / 128)) ||
       !fits_i32(bhq * (long long)n_ctx_q))
     return TF_ERR_TOO_LARGE;
@@ -910,27 +916,30 @@ namespace {
 // rows (2 x 1,048,576 floats = 8 MiB), written in full by every call's prep
 // kernel before use, so nothing needs clearing between calls.
 constexpr size_t kNoAllocWsBytes = size_t(8) << 20;
+constexpr long long kNoAllocRows = (long long)(kNoAllocWsBytes / (2 * sizeof(float)));
 __device__ __align__(256) float g_noalloc_ws[kNoAllocWsBytes / sizeof(float)];
 
-// Device address of g_noalloc_ws, looked up once per device with that device
-// current (host code only holds a stand-in symbol for it).
+// Device address of g_noalloc_ws for the current device (host code only holds
+// a stand-in symbol for it).  Only a successful lookup is cached: a failed one
+// (e.g. a first call made while the stream is being captured) is retried by
+// the next call.  Threads racing on the first lookup store the same address.
 void* noalloc_workspace(int* status) {
-  static std::once_flag flags[kMaxDevices];
-  static void* ptrs[kMaxDevices];
-  static int statuses[kMaxDevices];
+  static std::atomic<void*> ptrs[kMaxDevices];
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) {
     *status = TF_ERR_CUDA;
     return nullptr;
   }
-  std::call_once(flags[dev], [dev] {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_ws);
-    ptrs[dev] = e == cudaSuccess ? ptr : nullptr;
-    statuses[dev] = e == cudaSuccess ? TF_OK : TF_ERR_CUDA;
-  });
-  *status = statuses[dev];
-  return ptrs[dev];
+  void* ptr = ptrs[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_ws) != cudaSuccess || ptr == nullptr) {
+      *status = TF_ERR_CUDA;
+      return nullptr;
+    }
+    ptrs[dev].store(ptr, std::memory_order_release);
+  }
+  *status = TF_OK;
+  return ptr;
 }
 
 }  // namespace
@@ -945,9 +954,10 @@ extern "C" int tf_b200_flash_attn2_bwd_bf16_noalloc(const void* q, const void* k
   if (batch < 0 || n_heads_q < 0 || n_heads_kv < 0 || n_ctx_q < 0 || n_ctx_k < 0)
     return TF_ERR_INVALID_ARG;
   if (batch == 0 || n_heads_q == 0 || (n_ctx_q == 0 && n_ctx_k == 0)) return TF_OK;
-  if (n_ctx_q > 0 &&
-      bwd_workspace_bytes((long long)batch * n_heads_q, n_ctx_q) > kNoAllocWsBytes)
-    return TF_ERR_TOO_LARGE;
+  // rows of per-row statistics the call needs: B * Hq * round_up(Sq, 128)
+  // (both factors below 2^32, so the product cannot overflow)
+  const long long bhq = (long long)batch * n_heads_q;
+  if (!fits_i32(bhq) || bhq * bwd_sq_pad(n_ctx_q) > kNoAllocRows) return TF_ERR_TOO_LARGE;
   int st = TF_OK;
   void* ws = noalloc_workspace(&st);
   if (st != TF_OK) return st;

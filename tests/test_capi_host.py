@@ -138,3 +138,69 @@ def test_op_shape_inference_mirrors_reference():
     assert RopeOp(64, 1e4).param_shapes([(2, 3, 64)]) == []
     assert TransposeHeadsOp(4, 16).infer_output_shape([(10, 64)]) == (4, 10, 16)
     assert MergeHeadsOp(4, 16).infer_output_shape([(4, 10, 16)]) == (10, 64)
+
+
+def test_backward_size_limits_reject_without_overflow(native_lib):
+    """Head counts whose products would overflow 64-bit arithmetic are refused
+    before any device work (workspace size 0, TF_ERR_TOO_LARGE)."""
+    big = 1 << 30
+    assert _capi.raw("tf_b200_flash_attn2_bwd_workspace_size", big, big, 4096) == 0
+    assert _capi.raw("tf_b200_flash_attn2_bwd_workspace_size", 1, 1, 1) > 0
+    args = [FAKE] * 9
+    rc = _capi.raw("tf_b200_flash_attn2_bwd_bf16", *args, FAKE, big, big, big, 1 << 20,
+                   1 << 20, 128, 0.1, 1, None)
+    assert rc == _capi.TF_ERR_TOO_LARGE
+    for B, H, S in ((big, big, 4096), (1, 257, 4096), (1, 1, 1 << 30)):
+        rc = _capi.raw("tf_b200_flash_attn2_bwd_bf16_noalloc", *args, B, H, H, S, S, 128, 0.1, 1,
+                       None)
+        assert rc == _capi.TF_ERR_TOO_LARGE, (B, H, S)
+
+
+# C parameter type in the header -> its declaration in the Rust binding
+_C_TO_RUST = {
+    "const void*": "*const c_void", "void*": "*mut c_void", "const float*": "*const f32",
+    "float*": "*mut f32", "int": "c_int", "float": "f32", "size_t": "usize", "unsigned": "u32",
+    "const int*": "*const c_int", "const char*": "*const c_char",
+    "const void* const*": "*const *const c_void", "void* const*": "*const *mut c_void",
+}
+
+
+def _header_decls():
+    out = {}
+    for name in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if not name.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", name)).read()
+        for d in re.findall(r"^TF_API\s+([^;]*?\))\s*;", text, re.M | re.S):
+            d = " ".join(d.split())
+            m = re.match(r"(.+?)\b(tf_b200_\w+)\((.*)\)$", d)
+            params = []
+            if m.group(3) != "void":
+                for p in m.group(3).split(","):
+                    pm = re.match(r"(.*?)(\w+)$", p.strip())
+                    params.append((pm.group(2), _C_TO_RUST[pm.group(1).strip().replace(" *", "*")]))
+            out[m.group(2)] = (_C_TO_RUST[m.group(1).strip()], params)
+    return out
+
+
+def test_rust_binding_matches_header():
+    """rust/teeny-b200-sys declares every header entry point with the same
+    parameter names and types, in order (the crate is not compiled here)."""
+    src = open(os.path.join(ROOT, "rust", "teeny-b200-sys", "src", "lib.rs")).read()
+    block = src[src.index('unsafe extern "C" {'):]
+    block = block[:block.index("\n    }\n")]
+    rust = {}
+    for m in re.finditer(r"pub fn (tf_b200_\w+)\((.*?)\)\s*->\s*([^;]+);", block, re.S):
+        params = []
+        for p in " ".join(m.group(2).split()).split(","):
+            p = p.strip()
+            if p:
+                n, t = p.split(":", 1)
+                params.append((n.strip(), t.strip()))
+        rust[m.group(1)] = (m.group(3).strip(), params)
+    header = _header_decls()
+    assert set(rust) == set(header), set(rust) ^ set(header)
+    for name, decl in header.items():
+        assert rust[name] == decl, name
+    toml = open(os.path.join(ROOT, "rust", "teeny-b200-sys", "Cargo.toml")).read()
+    assert 'links = "teenyformers_b200"' in toml
