@@ -31,11 +31,18 @@ Default (fused) path, all on this library's sm_100a kernels:
                epilogue (N = 1)
 The fused path needs head_dim 128 and S % 128 == 0 (and B*S a multiple of
 128 * N with the peer all-reduce); other shapes, or ``fused=False``, take the
-separate-kernel path: the projections are plain torch.matmul (cuBLAS) calls
-followed by the separate RoPE/transpose, merge and SwiGLU kernels, and the
-all-reduce is NCCL through torch.distributed (`all_reduce`) or, with
-`peer_ar` (a tp.PeerAllReduceNorm), this library's all-reduce + residual +
-RMSNorm kernel loading the partials over NVLink.
+separate-kernel path, still entirely on this library's kernels: the
+projections run on the same tcgen05 GEMM without epilogue fusion, followed by
+the separate RoPE/transpose, merge and SwiGLU kernels, and the all-reduce is
+NCCL through torch.distributed (`all_reduce`) or, with `peer_ar` (a
+tp.PeerAllReduceNorm), this library's all-reduce + residual + RMSNorm kernel
+loading the partials over NVLink.  ``projections="cublas"`` swaps the
+separate path's projections for torch.matmul; it exists only as a named
+comparison arm for the benchmark and is never chosen implicitly.
+
+``LlamaModelTP`` stacks the layers and applies the final RMSNorm
+(``Llama::forward``, src/llama.rs:65-81, without the token embedding and the
+weight-tied lm_head, which are not on the attention path).
 """
 from __future__ import annotations
 
@@ -119,9 +126,15 @@ class LlamaLayerTP:
     the tensor-parallel group in place (identity for one rank)."""
 
     def __init__(self, cfg: LlamaLayerConfig, weights: dict, world: int = 1, all_reduce=None,
-                 peer_ar=None, fused: bool = True):
+                 peer_ar=None, fused: bool = True, projections: str = "ours"):
         if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.d_ff % world:
             raise ValueError("heads and d_ff must split evenly over the ranks")
+        if projections not in ("ours", "cublas"):
+            raise ValueError("projections must be 'ours' or 'cublas'")
+        if projections == "cublas" and fused:
+            raise ValueError("projections='cublas' is a comparison arm of the separate-kernel "
+                             "path: pass fused=False with it")
+        self.projections = projections
         self.cfg = cfg
         self.w = weights
         self.world = world
@@ -179,6 +192,21 @@ class LlamaLayerTP:
             return False
         return self.peer_ar is None or (B * S) % (128 * self.world) == 0
 
+    def _mm(self, a: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None) -> torch.Tensor:
+        """a @ weight.T (+ residual): this library's GEMM, or cuBLAS for the
+        explicitly requested comparison arm."""
+        if self.projections == "ours":
+            return ops.linear(a, weight, out=out, residual=residual)
+        y = torch.matmul(a, weight.t(), out=out)
+        return y if residual is None else y.add_(residual)
+
+    def _o_proj(self, o: torch.Tensor, S: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """merge_heads(o) @ Wo^T; head_dim 128 reads o in its own layout."""
+        if self.projections == "ours" and self.cfg.head_dim == 128:
+            return ops.linear(o, self.w["wo"], out=out, heads_seq=S)
+        return self._mm(ops.merge_heads(o), self.w["wo"], out=out)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.fused_ok(x.shape[0], x.shape[1]):
             return self._forward_fused(x)
@@ -186,9 +214,9 @@ class LlamaLayerTP:
         B, S, d = x.shape
         D = cfg.head_dim
         h = ops.rmsnorm(x, w["norm1"], cfg.eps)
-        q = torch.matmul(h, w["wq"].t())
-        k = torch.matmul(h, w["wk"].t())
-        v = torch.matmul(h, w["wv"].t())
+        q = self._mm(h, w["wq"])
+        k = self._mm(h, w["wk"])
+        v = self._mm(h, w["wv"])
         q = ops.rope_transpose(q.view(B, S, self.hq, D), cfg.rope_base, cfg.rope_style)
         k = ops.rope_transpose(k.view(B, S, self.hkv, D), cfg.rope_base, cfg.rope_style)
         v = ops.transpose_heads(v, self.hkv)
@@ -197,16 +225,55 @@ class LlamaLayerTP:
             # partials straight into the symmetric buffer; all-reduce + residual
             # + RMSNorm in one kernel; the layer output is the second h buffer
             ar = self.peer_ar
-            torch.matmul(ops.merge_heads(o), w["wo"].t(), out=ar.part.view(B, S, d))
+            self._o_proj(o, S, out=ar.part.view(B, S, d))
             x2, h2 = ar(0, x, w["norm2"], cfg.eps)
-            a = ops.swiglu(torch.matmul(h2.view(B, S, d), w["w_gate_up"].t()))
-            torch.matmul(a, w["w_down"].t(), out=ar.part.view(B, S, d))
+            a = ops.swiglu(self._mm(h2.view(B, S, d), w["w_gate_up"]))
+            self._mm(a, w["w_down"], out=ar.part.view(B, S, d))
             out, _ = ar(1, x2)
             return out.view(B, S, d)
-        attn = torch.matmul(ops.merge_heads(o), w["wo"].t())
+        attn = self._o_proj(o, S)
         self.all_reduce(attn)
         h2, x2 = ops.rmsnorm(attn, w["norm2"], cfg.eps, residual=x)
-        a = ops.swiglu(torch.matmul(h2, w["w_gate_up"].t()))
-        f = torch.matmul(a, w["w_down"].t())
+        a = ops.swiglu(self._mm(h2, w["w_gate_up"]))
+        if self.world == 1:
+            return self._mm(a, w["w_down"], residual=x2)
+        f = self._mm(a, w["w_down"])
         self.all_reduce(f)
         return x2 + f
+
+
+class LlamaModelTP:
+    """The Llama decoder stack on this rank's shards: ``n_layers`` pre-norm
+    blocks, then the final RMSNorm (src/llama.rs:65-81).  The token embedding
+    and the weight-tied lm_head around it are outside the attention path and
+    are not built; ``forward`` maps hidden states [B, S, d] to the normalised
+    hidden states the lm_head would read.
+
+    ``layer_weights`` holds one shard_weights(...) dict per layer; every other
+    argument is passed to each LlamaLayerTP.  With ``peer_ar`` each layer's
+    output is a view of the all-reduce's second h buffer, which the next layer
+    reads as its input before its own all-reduce writes that buffer again."""
+
+    def __init__(self, cfg: LlamaLayerConfig, layer_weights: list, norm_weight: torch.Tensor,
+                 **layer_kwargs):
+        if not layer_weights:
+            raise ValueError("the stack needs at least one layer")
+        self.cfg = cfg
+        self.layers = [LlamaLayerTP(cfg, w, **layer_kwargs) for w in layer_weights]
+        self.norm = norm_weight
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        for layer in self.layers:
+            x = layer.forward(x)
+        return ops.rmsnorm(x, self.norm, self.cfg.eps)
+
+
+def init_model_weights(cfg: LlamaLayerConfig, n_layers: int, seed: int, device,
+                       dtype=torch.bfloat16):
+    """Full (unsharded) weights of an n_layers stack: one init_full_weights
+    dict per layer (seeds seed, seed+1, ...) and the final norm's weight."""
+    layers = [init_full_weights(cfg, seed + i, device, dtype) for i in range(n_layers)]
+    g = torch.Generator(device=device).manual_seed(seed + n_layers)
+    norm = (1.0 + 0.02 * torch.randn(cfg.d_model, generator=g, device=device,
+                                      dtype=torch.float32)).to(dtype)
+    return layers, norm
