@@ -128,16 +128,55 @@ def test_config3_full_size_sampled_parity_and_properties(cuda_device):
     sum_do = do.float().sum(dim=2)
     assert (sum_dv - sum_do).abs().max().item() < 0.05 * sum_do.abs().max().item() + 0.5
     assert dk.float().sum(dim=2).abs().max().item() < 1.0
-    bsel, hsel = 5, 17
-    sl = lambda t: to_np(t[bsel:bsel + 1, hsel:hsel + 1])
-    o_ref, lse_ref = oracle.flash_attn2_fwd(sl(q), sl(k), sl(v), scale, True)
-    assert_bf16_close("O", sl(o), o_ref)
-    assert_bf16_close("LSE", sl(lse), lse_ref)
-    dq_ref, dk_ref, dv_ref = oracle.flash_attn2_bwd(sl(q), sl(k), sl(v), o_ref, sl(do), lse_ref,
-                                                    scale, True)
-    assert_bf16_close("dQ", sl(dq), dq_ref)
-    assert_bf16_close("dK", sl(dk), dk_ref)
-    assert_bf16_close("dV", sl(dv), dv_ref)
+    # one (b, h) slice in each 1/8 of the B*H heads -- the contiguous shard a
+    # rank owns at N = 8 is one batch entry here -- including the first and the
+    # last head of the whole tensor (shard edges at every N)
+    for bsel in range(B):
+        hsel = {0: 0, B - 1: H - 1}.get(bsel, (7 * bsel + 3) % H)
+        sl = lambda t: to_np(t[bsel:bsel + 1, hsel:hsel + 1])
+        o_ref, lse_ref = oracle.flash_attn2_fwd(sl(q), sl(k), sl(v), scale, True)
+        tag = f"b{bsel}h{hsel}"
+        assert_bf16_close("O " + tag, sl(o), o_ref)
+        assert_bf16_close("LSE " + tag, sl(lse), lse_ref)
+        dq_ref, dk_ref, dv_ref = oracle.flash_attn2_bwd(sl(q), sl(k), sl(v), o_ref, sl(do),
+                                                        lse_ref, scale, True)
+        assert_bf16_close("dQ " + tag, sl(dq), dq_ref)
+        assert_bf16_close("dK " + tag, sl(dk), dk_ref)
+        assert_bf16_close("dV " + tag, sl(dv), dv_ref)
+
+
+def test_config4_gqa_full_size_sampled_parity_and_properties(cuda_device):
+    """BASELINE config #4 (causal GQA forward, B=16, Hq=64, Hkv=8 -- eight query
+    heads per KV head -- S=8192, D=128) at full size.  Checked against the
+    oracle: one (b, KV group) slice with all eight of its query heads, on the
+    first and the last 256 query rows (the oracle's kv = h / (Hq / Hkv)
+    mapping is the contract; the reference layer is MHA).  On every head:
+      O[b, h, 0] == V[b, h / 8, 0] bit for bit (query 0 sees key 0 only), and
+      with V[k, 0] = k / S, O[q, 0] <= q / S (the causal mask)."""
+    B, Hq, Hkv, S, D = 16, 64, 8, 8192, 128
+    G = Hq // Hkv
+    scale = D ** -0.5
+    g = torch.Generator(device=cuda_device).manual_seed(4242)
+    q = torch.randn((B, Hq, S, D), generator=g, device=cuda_device, dtype=torch.bfloat16)
+    k = torch.randn((B, Hkv, S, D), generator=g, device=cuda_device, dtype=torch.bfloat16)
+    v = torch.randn((B, Hkv, S, D), generator=g, device=cuda_device, dtype=torch.bfloat16)
+    o, lse = tfb.flash_attn2_fwd(q, k, v, scale, True)
+    torch.cuda.synchronize()
+    kv_of = torch.arange(Hq, device=cuda_device) // G
+    assert torch.equal(o[:, :, 0, :], v[:, kv_of, 0, :])
+    bsel, gsel = 11, 5
+    qs = to_np(q[bsel:bsel + 1, gsel * G:(gsel + 1) * G])
+    ks = to_np(k[bsel:bsel + 1, gsel:gsel + 1])
+    vs = to_np(v[bsel:bsel + 1, gsel:gsel + 1])
+    os_, ls = to_np(o[bsel:bsel + 1, gsel * G:(gsel + 1) * G]), to_np(lse[bsel:bsel + 1, gsel * G:(gsel + 1) * G])
+    for lo, hi in ((0, 256), (S - 256, S)):
+        o_ref, lse_ref = oracle.flash_attn2_fwd(qs, ks, vs, scale, True, q_range=(lo, hi))
+        assert_bf16_close(f"O rows {lo}:{hi}", os_[:, :, lo:hi], o_ref[:, :, lo:hi])
+        assert_bf16_close(f"LSE rows {lo}:{hi}", ls[:, :, lo:hi], lse_ref[:, :, lo:hi])
+    pos = torch.arange(S, device=cuda_device, dtype=torch.float32) / S
+    v[..., 0] = pos.bfloat16()
+    o2, _ = tfb.flash_attn2_fwd(q, k, v, scale, True, out=o, lse=lse)
+    assert bool((o2[..., 0].float() <= pos.view(1, 1, S) * 1.01 + 1e-3).all())
 
 
 def test_causal_mask_property_full_size(cuda_device):

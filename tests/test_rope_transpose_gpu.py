@@ -85,13 +85,19 @@ def test_rope_transpose_small_vs_oracle(cuda_device, style):
     assert_bf16_close("rope_transpose^-1", to_np(dx), ref_back)
 
 
-def test_rope_transpose_config2_full_size(cuda_device):
-    """BASELINE config #2: x [4, 2048, 32, 128] bf16, theta 1e4, rotate-half."""
+@pytest.mark.parametrize("style", [tfb.TF_ROPE_ROTATE_HALF, tfb.TF_ROPE_INTERLEAVED],
+                         ids=["rotate_half", "interleaved"])
+def test_rope_transpose_config2_full_size(cuda_device, style):
+    """BASELINE config #2: x [4, 2048, 32, 128] bf16, theta 1e4; rotate-half (the
+    config's wording) and interleaved pairs (the reference's rope.rs)."""
     B, S, H, D = 4, 2048, 32, 128
     x = seeded_normal((B, S, H, D), seed=42, device=cuda_device)
-    y = tfb.rope_transpose(x, 10000.0, tfb.TF_ROPE_ROTATE_HALF)
-    ref = oracle.rope_transpose(to_np(x), math.log(10000.0), oracle.ROPE_ROTATE_HALF)
+    y = tfb.rope_transpose(x, 10000.0, style)
+    ref = oracle.rope_transpose(to_np(x), math.log(10000.0), style)
     assert_bf16_close("config2", to_np(y), ref)
+    # the inverse rotation + merge brings x back (to bf16 rounding of y)
+    back = tfb.rope_transpose(y, 10000.0, style, inverse=True)
+    assert_bf16_close("config2 inverse", to_np(back), to_np(x))
     # transpose itself is bit-exact at full size
     t = tfb.transpose_heads(x.view(B, S, H * D), H)
     assert torch.equal(t.view(torch.int16), x.permute(0, 2, 1, 3).contiguous().view(torch.int16))
