@@ -28,3 +28,37 @@ def test_bounded_wait_times_out_and_reports(cuda_device, tmp_path):
     ok, abort_flag, status, after = res.cpu().tolist()
     assert ok == 0 and abort_flag == 1 and status == 77 and after == 1
     assert 1.5 < elapsed < 30
+
+
+def test_peer_allreduce_barrier_times_out_and_reports(cuda_device):
+    """The tensor-parallel all-reduce's cross-rank barrier, run as rank 0 of a
+    2-rank group on one GPU where 'rank 1' is a local signal pad nothing ever
+    writes: the flag wait gives up after its 2 s bound, the kernel returns,
+    the device status holds the barrier's site code (801), and the context
+    keeps working (a 1-rank call on the same buffers then completes)."""
+    import teenyformers_b200 as tfb
+    from teenyformers_b200 import _capi
+    rows, cols = 256, 512
+    pad_u32 = 256 + 2 * 128 * 8
+    parts = [torch.randn(rows, cols, device=cuda_device).bfloat16() for _ in range(2)]
+    hs = [torch.zeros(rows, cols, device=cuda_device, dtype=torch.bfloat16) for _ in range(2)]
+    pads = [torch.zeros(pad_u32, device=cuda_device, dtype=torch.int32) for _ in range(2)]
+    dev_ptrs = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64,
+                                       device=cuda_device)
+    src, hp, sp = dev_ptrs(parts), dev_ptrs(hs), dev_ptrs(pads)
+    p = lambda t: ctypes.c_void_p(0 if t is None else t.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    assert tfb.device_status(clear=True) == 0
+    t0 = time.time()
+    _capi.call("tf_b200_allreduce_residual_rmsnorm_bf16", p(src), p(hp), p(sp), None, None, None,
+               0, 2, rows, cols, 1e-5, 1, stream)
+    torch.cuda.synchronize()
+    elapsed = time.time() - t0
+    assert tfb.device_status(clear=True) == 801
+    assert 1.5 < elapsed < 30
+    # the context is usable: a one-rank all-reduce (epoch 2) completes, h = partial
+    _capi.call("tf_b200_allreduce_residual_rmsnorm_bf16", p(src), p(hp), p(sp), None, None, None,
+               0, 1, rows, cols, 1e-5, 2, stream)
+    torch.cuda.synchronize()
+    assert tfb.device_status(clear=True) == 0
+    assert torch.equal(hs[0], parts[0])
