@@ -122,7 +122,7 @@ class DecoderBlockTP:
 
     def _o_proj(self, o: torch.Tensor, weight: torch.Tensor, S: int,
                 residual: torch.Tensor | None = None) -> torch.Tensor:
-        if self.cfg.head_dim == 128:
+        if self.cfg.head_dim == 128 and S % 128 == 0:  # o read in its own layout
             return ops.linear(o, weight, heads_seq=S, residual=residual)
         return ops.linear(ops.merge_heads(o), weight, residual=residual)
 

@@ -202,8 +202,9 @@ class LlamaLayerTP:
         return y if residual is None else y.add_(residual)
 
     def _o_proj(self, o: torch.Tensor, S: int, out: torch.Tensor | None = None) -> torch.Tensor:
-        """merge_heads(o) @ Wo^T; head_dim 128 reads o in its own layout."""
-        if self.projections == "ours" and self.cfg.head_dim == 128:
+        """merge_heads(o) @ Wo^T; head_dim 128 and S % 128 == 0 read o in its own
+        layout (the GEMM's heads-layout A loads whole 128-row blocks of a head)."""
+        if self.projections == "ours" and self.cfg.head_dim == 128 and S % 128 == 0:
             return ops.linear(o, self.w["wo"], out=out, heads_seq=S)
         return self._mm(ops.merge_heads(o), self.w["wo"], out=out)
 

@@ -23,6 +23,8 @@ def fake_ops(monkeypatch):
         monkeypatch.setattr(ops, name, f)
 
     def linear(x, w, out=None, heads_seq=0, residual=None):
+        # the GEMM's host check: heads-layout A needs 128-row blocks per head
+        assert heads_seq % 128 == 0 and x.shape[-1] == 128 if heads_seq else True
         lead = (x.shape[0], heads_seq) if heads_seq else tuple(x.shape[:-1])
         return torch.zeros(lead + (w.shape[0],), dtype=x.dtype)
 
