@@ -40,6 +40,19 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
       "r"(smem_src), "r"(c0), "r"(c1)
       : "memory");
 }
+// TMA tensor store of a shared-memory tile (layout as the map's swizzle) to
+// global; completion tracked by bulk async-groups.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t smem_src, int c0,
+                                             int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -51,9 +64,6 @@ __device__ __forceinline__ void bulk_wait_group0() {
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 // AND of `v` over the `nthreads` threads of named barrier `id` (all of them
 // get the same answer, so they take the same branch afterwards).
@@ -167,7 +177,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                               const __grid_constant__ CUtensorMap tm_do,
                               const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v,
-                              const __grid_constant__ CUtensorMap tm_dqacc, const BwdParams p) {
+                              const __grid_constant__ CUtensorMap tm_dqacc,
+                              const __grid_constant__ CUtensorMap tm_dk,
+                              const __grid_constant__ CUtensorMap tm_dv, const BwdParams p) {
   using C = BwdFusedCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
@@ -435,6 +447,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     // dS^T row `row` in the MN-major SW128 tile read by the dQ MMA: half ewg,
     // 16-byte chunk c of the row at physical chunk c ^ (row & 7)
     const uint32_t ds_row = sbase + C::OFF_DS + ewg * C::HALF_BYTES + row * 128;
+    const bool epi_issuer = (warp & 3) == 0 && lane == 0;  // first thread of the warpgroup
     bool ok = true;
     int kv_items = 0, g0 = 0;
     for (int k = 0; ok; ++k) {
@@ -544,27 +557,57 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         mbar_arrive_warp(bar(FB2_DSFULL));
       }
       if (!ok) break;
-      // ---- epilogue: warpgroup 0 writes dV, 1 writes dK (= acc * scale); the
-      // accumulators are released once read, while the stores drain
+      // ---- epilogue: warpgroup 0 writes dV, 1 writes dK (= acc * scale).  Each
+      // 64-column half goes bf16 into this warpgroup's half of the dS tile
+      // (free: the item's last dQ MMA has read it), laid out as the output
+      // map's 128-byte swizzle, and leaves in one TMA tensor store (rows past
+      // Sk are clipped by the map).  The accumulators are released once read.
       ok = __all_sync(0xffffffffu, mbar_wait(bar(FB2_ACC), kv_items & 1, abort_flag, 634));
       if (!ok) break;
       tc_fence_after();
       const uint32_t acc_col = ewg == 0 ? C::TM_DV : C::TM_DK;
       const float mul = ewg == 0 ? 1.0f : p.scale;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + acc_col + c * 32, r);
-        tmem_wait_ld();
-        if (c == D / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive_warp(bar(FB2_ACCFREE));
+      const CUtensorMap* out_map = ewg == 0 ? &tm_dv : &tm_dk;
+      const uint32_t stage = sbase + C::OFF_DS + ewg * C::HALF_BYTES;
+      const uint32_t stage_row = stage + row * 128;
+      for (int hh = 0; hh < C::HALVES; ++hh) {
+        if (hh > 0) {  // the previous half's store has read the staging tile
+          if (epi_issuer) bulk_wait_group_read0();
+          named_bar_sync(2 + ewg, 128);
         }
-        if (valid) store_row_chunk_bf16(out_row + c * 32, r, mul);
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + acc_col + hh * 64 + c * 32, r);
+          tmem_wait_ld();
+          if (hh == C::HALVES - 1 && c == 1) {
+            tc_fence_before();
+            mbar_arrive_warp(bar(FB2_ACCFREE));
+          }
+          uint32_t wv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            wv[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * mul, __uint_as_float(r[2 * i + 1]) * mul);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            st_shared_v4(stage_row + ((uint32_t(c * 4 + v) ^ uint32_t(row & 7)) << 4), wv[4 * v],
+                         wv[4 * v + 1], wv[4 * v + 2], wv[4 * v + 3]);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(2 + ewg, 128);
+        if (epi_issuer) {
+          tma_store_3d(out_map, stage, hh * 64, item.k0, item.bh_kv);
+          bulk_commit_group();
+        }
       }
+      // the dS tile is rewritten by the next item's first tile: its stores must
+      // have read the staging first
+      if (epi_issuer) bulk_wait_group_read0();
+      named_bar_sync(2 + ewg, 128);
       ++kv_items;
       g0 += item.n_tiles;
     }
+    if (epi_issuer) bulk_wait_group0();  // dK / dV stores complete before the CTA exits
   } else {
     // ------------- dQ reduction: thread = query row of the tile
     if constexpr (D == 128) regs_inc<kRegsReduce>();

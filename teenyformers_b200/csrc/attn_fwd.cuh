@@ -45,6 +45,7 @@ struct FwdParams {
   float scale_log2;  // softmax_scale * log2(e)
   int causal;
   int heavy_first;  // item order: all heads' heaviest pairs first (K/V fit in L2)
+  int tail_heads;   // head-major order: the last tail_heads heads go heaviest pair first
 };
 
 template <int D>
@@ -90,7 +91,10 @@ __device__ __forceinline__ void mbar_drain_wait(uint32_t bar, uint32_t parity, i
 // CTAs running at any time share a few heads' K/V in L2), heavy (late) pairs
 // first within a head when causal.  With heavy_first (causal, and all K/V
 // small enough to stay in L2): pair-major from the heaviest pair down, so the
-// boustrophedon rounds approximate longest-first scheduling.  Each role
+// boustrophedon rounds approximate longest-first scheduling.  Otherwise, when
+// causal, the last tail_heads heads (about two rounds of items, whose K/V fit
+// in L2) are taken pair-major in the same way, so the final, partial round
+// holds only light items and the CTAs finish close together.  Each role
 // derives the same values from w.
 struct FwdItem {
   int bh, bh_kv, q0, nkv0, nkv1, n_iter;
@@ -98,9 +102,13 @@ struct FwdItem {
 __device__ __forceinline__ FwdItem fwd_item(const FwdParams& p, int w) {
   FwdItem it;
   int pair;
+  const int tail0 = (p.BHq - p.tail_heads) * p.n_pairs;  // first item of the tail window
   if (p.heavy_first) {
     pair = p.n_pairs - 1 - w / p.BHq;
     it.bh = w % p.BHq;
+  } else if (w >= tail0) {
+    pair = p.n_pairs - 1 - (w - tail0) / p.tail_heads;
+    it.bh = p.BHq - p.tail_heads + (w - tail0) % p.tail_heads;
   } else {
     it.bh = w / p.n_pairs;
     pair = w % p.n_pairs;

@@ -101,6 +101,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// Named barrier over `nthreads` threads (whole warps) of the CTA; id 0 is
+// __syncthreads.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // One lane of a converged warp (elect.sync).  Producer / MMA warps run their
 // loops with all 32 lanes so loop state stays warp-uniform, and only the
 // elected lane issues TMA copies, MMAs and commits.
@@ -114,7 +120,9 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
-// mbar_wait by every lane of a warp, with a warp-uniform result.
+// mbar_wait by every lane of a warp, with a warp-uniform result.  (Polling
+// from lane 0 alone, with the other lanes parked in __syncwarp, measured
+// about twice as slow per backward tile: the diverged waiter resumes late.)
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity,
                                                volatile int* abort_flag, int site) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));

@@ -247,6 +247,10 @@ extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const 
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   const dim3 grid(persistent_grid(bhq * n_pairs));
+  // about two rounds of items at the end taken heaviest pair first (whole heads)
+  prm.tail_heads = (causal && !prm.heavy_first)
+                       ? (int)std::min<long long>(bhq, (2LL * grid.x + n_pairs - 1) / n_pairs)
+                       : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128)
     fa_fwd_sm100_kernel<128><<<grid, FwdCfg<128>::kThreads, FwdCfg<128>::SMEM_BYTES, st>>>(
@@ -342,21 +346,24 @@ int bwd_bf16_impl(const void* q, const void* k, const void* v, const void* o, co
   const dim3 grid_kv((unsigned)(bhkv * prm.n_kt));
   if (fused) {
     if (!fits_i32(rows)) return TF_ERR_TOO_LARGE;  // accumulator row index is int
-    CUtensorMap tacc;
-    if (!make_f32_acc_map(&tacc, dq_acc, head_dim, rows)) return TF_ERR_CUDA;
+    CUtensorMap tacc, tdk, tdv;
+    if (!make_f32_acc_map(&tacc, dq_acc, head_dim, rows) ||
+        !make_bf16_map(&tdk, dk, head_dim, n_ctx_k, (int)bhkv, 128) ||
+        !make_bf16_map(&tdv, dv, head_dim, n_ctx_k, (int)bhkv, 128))
+      return TF_ERR_CUDA;
     const long long out_rows = bhq * (long long)n_ctx_q;
     const long long groups = out_rows * (head_dim / 8);
     const unsigned cgrid = (unsigned)std::min<long long>((groups + 255) / 256, 148LL * 16);
     if (head_dim == 128) {
       fa_bwd_fused_sm100_kernel<128><<<persistent_grid(prm.n_items), kFusedThreads,
                                        BwdFusedCfg<128>::SMEM_BYTES, st>>>(tq, tdo, tk, tv, tacc,
-                                                                           prm);
+                                                                           tdk, tdv, prm);
       fa_bwd_dq_convert_kernel<128><<<cgrid, 256, 0, st>>>(
           dq_acc, prm.dq, n_ctx_q, sq_pad, out_rows, softmax_scale);
     } else {
       fa_bwd_fused_sm100_kernel<64><<<persistent_grid(prm.n_items), kFusedThreads,
                                       BwdFusedCfg<64>::SMEM_BYTES, st>>>(tq, tdo, tk, tv, tacc,
-                                                                         prm);
+                                                                         tdk, tdv, prm);
       fa_bwd_dq_convert_kernel<64><<<cgrid, 256, 0, st>>>(
           dq_acc, prm.dq, n_ctx_q, sq_pad, out_rows, softmax_scale);
     }

@@ -54,3 +54,4 @@ def assert_bf16_close_scaled(name, got, ref, tol=BF16_MAX_ABS, rl2=BF16_REL_L2):
     r = rel_l2(got, ref) if got.size else 0.0
     assert err <= tol and r <= rl2, f"{name}: scaled max-abs {err:.3e} (<= {tol}), rel-L2 {r:.3e} (<= {rl2})"
     return err, r
+

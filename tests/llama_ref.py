@@ -105,28 +105,43 @@ def decoder_ref_fp32(tgt, enc, blocks, norm, cfg, n_heads_local, n_kv_local,
     return torch.from_numpy(y)
 
 
-def layer_rows_ref_fp32(x, w, cfg, n_heads, n_kv, q_lo, q_hi):
+def _rb(t):
+    """Rounds an fp32 torch tensor or numpy array to bf16 and back (round to nearest even)."""
+    if isinstance(t, np.ndarray):
+        return torch.from_numpy(np.ascontiguousarray(t)).to(torch.bfloat16).float().numpy()
+    return t.to(torch.bfloat16).float()
+
+
+def layer_rows_ref_fp32(x, w, cfg, n_heads, n_kv, q_lo, q_hi, bf16_points=False):
     """Rows [q_lo, q_hi) of the single-rank layer's output, for full-size
     checks: K and V (and Q, for the RoPE positions) are projected for every
     token, attention and everything after it only for the sampled rows.
-    x [B, S, d] fp32 torch (CPU); returns [B, q_hi - q_lo, d]."""
+    x [B, S, d] fp32 torch (CPU); returns [B, q_hi - q_lo, d].
+
+    With ``bf16_points`` the fp32 arithmetic is unchanged but the activations
+    are rounded to bf16 where the fused layer stores them (h, q/k after RoPE,
+    v, the attention output, o_proj's output, x2 and h2 from the fp32
+    residual sum, the SwiGLU output, down_proj's output and y), so what remains
+    is the kernels' own error (accumulation order, bf16 P inside attention)."""
+    rb = _rb if bf16_points else (lambda t: t)
     B, S, d = x.shape
     D = cfg.head_dim
     f = {k: v.float().cpu() for k, v in w.items()}
     h, _ = oracle.rmsnorm(x.numpy(), f["norm1"].numpy(), cfg.eps)
-    h = torch.from_numpy(h)
+    h = torch.from_numpy(rb(h))
     ln_base = math.log(cfg.rope_base)
-    q = oracle.rope_transpose((h @ f["wq"].t()).reshape(B, S, n_heads, D).numpy(), ln_base,
-                              cfg.rope_style)
-    k = oracle.rope_transpose((h @ f["wk"].t()).reshape(B, S, n_kv, D).numpy(), ln_base,
-                              cfg.rope_style)
-    v = np.ascontiguousarray((h @ f["wv"].t()).reshape(B, S, n_kv, D).numpy().transpose(0, 2, 1, 3))
+    q = rb(oracle.rope_transpose((h @ f["wq"].t()).reshape(B, S, n_heads, D).numpy(), ln_base,
+                                 cfg.rope_style))
+    k = rb(oracle.rope_transpose((h @ f["wk"].t()).reshape(B, S, n_kv, D).numpy(), ln_base,
+                                 cfg.rope_style))
+    v = rb(np.ascontiguousarray((h @ f["wv"].t()).reshape(B, S, n_kv, D).numpy().transpose(0, 2, 1, 3)))
     o, _ = oracle.flash_attn2_fwd(q, k, v, 1.0 / math.sqrt(D), True, q_range=(q_lo, q_hi))
-    o = o[:, :, q_lo:q_hi]
+    o = rb(o[:, :, q_lo:q_hi])
     o = torch.from_numpy(np.ascontiguousarray(o.transpose(0, 2, 1, 3)).reshape(B, q_hi - q_lo,
                                                                                n_heads * D))
-    attn = o @ f["wo"].t()
+    attn = rb(o @ f["wo"].t())
     xr = x[:, q_lo:q_hi].contiguous().numpy()
     h2, x2 = oracle.rmsnorm(attn.numpy(), f["norm2"].numpy(), cfg.eps, residual=xr)
-    a = torch.from_numpy(oracle.swiglu((torch.from_numpy(h2) @ f["w_gate_up"].t()).numpy()))
-    return torch.from_numpy(x2) + a @ f["w_down"].t()
+    h2, x2 = rb(h2), rb(x2)
+    a = rb(torch.from_numpy(oracle.swiglu((torch.from_numpy(h2) @ f["w_gate_up"].t()).numpy())))
+    return rb(torch.from_numpy(x2) + rb(a @ f["w_down"].t()))

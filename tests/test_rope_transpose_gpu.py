@@ -13,7 +13,7 @@ import torch
 
 import oracle
 import teenyformers_b200 as tfb
-from tests.helpers import F32_ABS, assert_bf16_close, seeded_normal, to_np
+from tests.helpers import F32_ABS, assert_bf16_close, assert_bf16_close_scaled, seeded_normal, to_np
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -95,9 +95,10 @@ def test_rope_transpose_config2_full_size(cuda_device, style):
     y = tfb.rope_transpose(x, 10000.0, style)
     ref = oracle.rope_transpose(to_np(x), math.log(10000.0), style)
     assert_bf16_close("config2", to_np(y), ref)
-    # the inverse rotation + merge brings x back (to bf16 rounding of y)
+    # the inverse rotation + merge brings x back, to two bf16 roundings (of y and
+    # of the result): relative above magnitude 1, where |x| reaches ~5.5 here
     back = tfb.rope_transpose(y, 10000.0, style, inverse=True)
-    assert_bf16_close("config2 inverse", to_np(back), to_np(x))
+    assert_bf16_close_scaled("config2 inverse", to_np(back), to_np(x))
     # transpose itself is bit-exact at full size
     t = tfb.transpose_heads(x.view(B, S, H * D), H)
     assert torch.equal(t.view(torch.int16), x.permute(0, 2, 1, 3).contiguous().view(torch.int16))
