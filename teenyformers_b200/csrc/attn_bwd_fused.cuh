@@ -40,30 +40,8 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
       "r"(smem_src), "r"(c0), "r"(c1)
       : "memory");
 }
-// TMA tensor store of a shared-memory tile (layout as the map's swizzle) to
-// global; completion tracked by bulk async-groups.
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t smem_src, int c0,
-                                             int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(smem_src), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_wait_group_read0() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_commit_group() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
 __device__ __forceinline__ void bulk_wait_group_read1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_group0() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 // AND of `v` over the `nthreads` threads of named barrier `id` (all of them
 // get the same answer, so they take the same branch afterwards).
@@ -86,12 +64,6 @@ __device__ __forceinline__ void regs_inc() {
 template <int N>
 __device__ __forceinline__ void regs_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
-               "r"(d)
-               : "memory");
 }
 
 constexpr int kFusedThreads = 512;

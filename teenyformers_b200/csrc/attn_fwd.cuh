@@ -45,7 +45,6 @@ struct FwdParams {
   float scale_log2;  // softmax_scale * log2(e)
   int causal;
   int heavy_first;  // item order: all heads' heaviest pairs first (K/V fit in L2)
-  int tail_heads;   // head-major order: the last tail_heads heads go heaviest pair first
 };
 
 template <int D>
@@ -58,7 +57,10 @@ struct FwdCfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
   static constexpr int OFF_V = OFF_K + KSTAGES * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_V + KSTAGES * TILE_BYTES;
+  // epilogue staging: per query tile one 128-row x 64-column bf16 half of O
+  // (128-byte swizzle, the O map's box), written out by TMA stores
+  static constexpr int OFF_STG = OFF_V + KSTAGES * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + 2 * HALF_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // barriers + 1 KB align slack
   __device__ static constexpr uint32_t tm_s(int t) { return uint32_t(t) * 128u; }
   __device__ static constexpr uint32_t tm_o(int t) { return 256u + uint32_t(t) * D; }
@@ -91,10 +93,7 @@ __device__ __forceinline__ void mbar_drain_wait(uint32_t bar, uint32_t parity, i
 // CTAs running at any time share a few heads' K/V in L2), heavy (late) pairs
 // first within a head when causal.  With heavy_first (causal, and all K/V
 // small enough to stay in L2): pair-major from the heaviest pair down, so the
-// boustrophedon rounds approximate longest-first scheduling.  Otherwise, when
-// causal, the last tail_heads heads (about two rounds of items, whose K/V fit
-// in L2) are taken pair-major in the same way, so the final, partial round
-// holds only light items and the CTAs finish close together.  Each role
+// boustrophedon rounds approximate longest-first scheduling.  Each role
 // derives the same values from w.
 struct FwdItem {
   int bh, bh_kv, q0, nkv0, nkv1, n_iter;
@@ -102,13 +101,9 @@ struct FwdItem {
 __device__ __forceinline__ FwdItem fwd_item(const FwdParams& p, int w) {
   FwdItem it;
   int pair;
-  const int tail0 = (p.BHq - p.tail_heads) * p.n_pairs;  // first item of the tail window
   if (p.heavy_first) {
     pair = p.n_pairs - 1 - w / p.BHq;
     it.bh = w % p.BHq;
-  } else if (w >= tail0) {
-    pair = p.n_pairs - 1 - (w - tail0) / p.tail_heads;
-    it.bh = p.BHq - p.tail_heads + (w - tail0) % p.tail_heads;
   } else {
     it.bh = w / p.n_pairs;
     pair = w % p.n_pairs;
@@ -145,7 +140,8 @@ template <int D>
 __global__ void __launch_bounds__(320, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -379,6 +375,9 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t tS = tmem + lane_base + C::tm_s(t);
     const uint32_t tO = tmem + lane_base + C::tm_o(t);
     const float sl2 = p.scale_log2;
+    const uint32_t stage = sbase + C::OFF_STG + t * C::HALF_BYTES;
+    const uint32_t stage_row = stage + row * 128;
+    const bool epi_issuer = wq == 0 && lane == 0;  // first thread of the tile's warpgroup
     bool ok = true;
     int st_t = 0, no_t = 0;  // this tile's steps / items with work so far
     for (int k = 0; ok; ++k) {
@@ -471,40 +470,51 @@ __global__ void __launch_bounds__(320, 1)
         m = m_use;
       }
       if (!ok) break;
-      // ---- epilogue: O / l (bf16) and LSE; O_t is released to the next item's
-      // first P V MMA once read, while the stores drain
+      // ---- epilogue: O / l (bf16) and LSE.  Each 64-column half of O_t is
+      // staged in this tile's 16 KB buffer (128-byte swizzle) and leaves in one
+      // TMA tensor store (rows past Sq are clipped by the map); O_t is released
+      // to the next item's first P V MMA once read out of TMEM.
       ok = __all_sync(0xffffffffu, mbar_wait(bar(FB_ODONE + t), uint32_t(no_t) & 1u, abort_flag,
                                              310 + t));
       if (!ok) break;
       tc_fence_after();
       const float inv_l = 1.0f / l;
-      const bool valid = q_idx < p.Sq;
-      __nv_bfloat16* orow_g = p.o + ((size_t)it.bh * p.Sq + (valid ? q_idx : 0)) * D;
+      for (int hh = 0; hh < C::HALVES; ++hh) {
+        // the previous store out of this buffer (of this item or the last one)
+        // has read it
+        if (epi_issuer) bulk_wait_group_read0();
+        named_bar_sync(1 + t, 128);
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t orow[32];
-        tmem_ld32(tO + c * 32, orow);
-        tmem_wait_ld();
-        if (c == D / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive_warp(bar(FB_OFREE + t));
+        for (int c = 0; c < 2; ++c) {
+          uint32_t orow[32];
+          tmem_ld32(tO + hh * 64 + c * 32, orow);
+          tmem_wait_ld();
+          if (hh == C::HALVES - 1 && c == 1) {
+            tc_fence_before();
+            mbar_arrive_warp(bar(FB_OFREE + t));
+          }
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack_bf16x2(__uint_as_float(orow[2 * i]) * inv_l,
+                               __uint_as_float(orow[2 * i + 1]) * inv_l);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            st_shared_v4(stage_row + ((uint32_t(c * 4 + v) ^ uint32_t(row & 7)) << 4), w[4 * v],
+                         w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
         }
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          w[i] = pack_bf16x2(__uint_as_float(orow[2 * i]) * inv_l,
-                             __uint_as_float(orow[2 * i + 1]) * inv_l);
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(orow_g + c * 32);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            dst[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
+        fence_proxy_async_smem();
+        named_bar_sync(1 + t, 128);
+        if (epi_issuer) {
+          tma_store_3d(&tm_o, stage, hh * 64, qs, it.bh);
+          bulk_commit_group();
         }
       }
-      if (valid) p.lse[(size_t)it.bh * p.Sq + q_idx] = (m + lg2_approx(l)) * 0.6931471805599453f;
+      if (q_idx < p.Sq) p.lse[(size_t)it.bh * p.Sq + q_idx] = (m + lg2_approx(l)) * 0.6931471805599453f;
       st_t += nk;
       ++no_t;
     }
+    if (epi_issuer) bulk_wait_group0();  // O stores complete before the CTA exits
   }
 
   // ---- teardown ----

@@ -228,10 +228,11 @@ extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const 
     return TF_ERR_TOO_LARGE;
   if (int st = ensure_device_setup()) return st;
 
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   if (!make_bf16_map(&tq, q, head_dim, n_ctx_q, (int)bhq, 128) ||
       !make_bf16_map(&tk, k, head_dim, n_ctx_k, batch * n_heads_kv, 128) ||
-      !make_bf16_map(&tv, v, head_dim, n_ctx_k, batch * n_heads_kv, 128))
+      !make_bf16_map(&tv, v, head_dim, n_ctx_k, batch * n_heads_kv, 128) ||
+      !make_bf16_map(&to, o, head_dim, n_ctx_q, (int)bhq, 128))
     return TF_ERR_CUDA;
   FwdParams prm;
   prm.o = static_cast<__nv_bfloat16*>(o);
@@ -247,17 +248,13 @@ extern "C" int tf_b200_flash_attn2_fwd_bf16(const void* q, const void* k, const 
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.causal = causal ? 1 : 0;
   const dim3 grid(persistent_grid(bhq * n_pairs));
-  // about two rounds of items at the end taken heaviest pair first (whole heads)
-  prm.tail_heads = (causal && !prm.heavy_first)
-                       ? (int)std::min<long long>(bhq, (2LL * grid.x + n_pairs - 1) / n_pairs)
-                       : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128)
     fa_fwd_sm100_kernel<128><<<grid, FwdCfg<128>::kThreads, FwdCfg<128>::SMEM_BYTES, st>>>(
-        tq, tk, tv, prm);
+        tq, tk, tv, to, prm);
   else
     fa_fwd_sm100_kernel<64><<<grid, FwdCfg<64>::kThreads, FwdCfg<64>::SMEM_BYTES, st>>>(
-        tq, tk, tv, prm);
+        tq, tk, tv, to, prm);
   return launch_status();
 }
 
