@@ -100,7 +100,7 @@ enum BwdFusedBar {
   FB2_KVFULL = 0, FB2_KVEMPTY = 1, FB2_QFULL = 2, FB2_QEMPTY = 4, FB2_DOFULL = 6,
   FB2_DOEMPTY = 7, FB2_SFULL = 8, FB2_PFULL = 9, FB2_DPFULL = 10, FB2_DSFULL = 11,
   FB2_DQFULL = 12, FB2_DQEMPTY = 13, FB2_ACC = 14, FB2_ACCFREE = 15, FB2_ITEMFULL = 16,
-  FB2_ITEMEMPTY = 20, FB2_DRAIN = 24, FB2_COUNT = 25
+  FB2_ITEMEMPTY = 20, FB2_DRAIN = 24, FB2_DSSMEM = 25, FB2_COUNT = 26
 };
 constexpr int kItemRing = 4;      // work items the TMA warp may fetch ahead
 constexpr int kItemConsumers = 13;  // MMA warp + 8 elementwise warps + 4 reduction warps
@@ -180,7 +180,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     mbar_init(bar(FB2_SFULL), 1);
     mbar_init(bar(FB2_PFULL), 8);  // one arrival per elementwise warp
     mbar_init(bar(FB2_DPFULL), 1);
-    mbar_init(bar(FB2_DSFULL), 8);
+    mbar_init(bar(FB2_DSFULL), 8);   // dS^T packed in TMEM (dK's A operand)
+    mbar_init(bar(FB2_DSSMEM), 8);   // dS tile in shared memory (dQ's A operand)
     mbar_init(bar(FB2_DQFULL), 1);
     mbar_init(bar(FB2_DQEMPTY), 4);  // one per reduction warp
     mbar_init(bar(FB2_ACC), 1);
@@ -381,6 +382,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           tc_fence_after();
           issue_acc(tmem + C::TM_DK, tmem + C::TM_DPT,
                     desc_adv(m_q0, (g & 1) * C::TILE_BYTES), it > 0, FB2_QEMPTY + (g & 1));
+          ok = mbar_wait_warp(bar(FB2_DSSMEM), g & 1, abort_flag, 625);
+          if (!ok) break;
+          tc_fence_after();
           issue_dq();
           if (!more) {
             if (elect_one()) {
@@ -523,10 +527,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           st_shared_v4(ds_row + (((ch + 1) ^ uint32_t(row & 7)) << 4), dk[4], dk[5], dk[6],
                        dk[7]);
         }
+        // dK reads dS^T from TMEM: released before the shared-memory proxy fence
+        // that only the dQ MMA (dS from the shared tile) needs
         tmem_wait_st();
-        fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive_warp(bar(FB2_DSFULL));
+        fence_proxy_async_smem();
+        mbar_arrive_warp(bar(FB2_DSSMEM));
       }
       if (!ok) break;
       // ---- epilogue: warpgroup 0 writes dV, 1 writes dK (= acc * scale).  Each
