@@ -74,8 +74,10 @@ __global__ void __launch_bounds__(256)
                      int in_layout, int out_layout, float coef, int rows_per_cta) {
   constexpr int EPV = Vec16<T>::N;  // elements per 16-byte vector
   const int s = blockIdx.x;
-  // vectors handled per thread per row: 1 (interleaved) or 2 (rotate-half)
-  const int cpr = STYLE == 0 ? D / EPV : D / (2 * EPV);
+  // each thread handles two 16-byte vectors of a row, c and c + D / (2 EPV):
+  // the partner halves for rotate-half; for interleaved pairs (which sit
+  // inside a vector) the same layout keeps both styles' accesses identical
+  const int cpr = D / (2 * EPV);
   const int rows_per_pass = blockDim.x / cpr;
   const int c = threadIdx.x % cpr;
   const int r0 = threadIdx.x / cpr;
@@ -88,10 +90,9 @@ __global__ void __launch_bounds__(256)
     const int b = r / H, h = r % H;
     return reinterpret_cast<const uint4*>(x + row_offset(in_layout, b, s, h, S, H) * row_elems);
   };
-  // The first kPre rows' loads go out before the angles are computed, so the
-  // memory system is busy while the CTA evaluates them (8 single vectors for
-  // interleaved pairs, 4 vector pairs for rotate-half).
-  constexpr int kPre = STYLE == 0 ? 8 : 4;
+  // The first kPre rows' loads (vector pairs) go out before the angles are
+  // computed, so the memory system is busy while the CTA evaluates them.
+  constexpr int kPre = 4;
   const bool active = r0 < rows_per_pass;
   uint4 pre0[kPre], pre1[kPre];
 #pragma unroll
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(256)
     if (active && r < row_hi) {
       const uint4* sp = src_of(r);
       pre0[j] = __ldcs(sp + c);
-      pre1[j] = STYLE == 1 ? __ldcs(sp + c + half_vecs) : pre0[j];
+      pre1[j] = __ldcs(sp + c + half_vecs);
     }
   }
 
@@ -116,11 +117,15 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   if (!active) return;
-  constexpr int NP = STYLE == 0 ? EPV / 2 : EPV;
-  float cs[NP], sn[NP];
+  // this thread's EPV angles: interleaved, the pairs of vector c then of
+  // vector c + half_vecs; rotate-half, pairs c EPV .. c EPV + EPV - 1
+  float cs[EPV], sn[EPV];
 #pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const float2 a = ang[STYLE == 0 ? c * (EPV / 2) + i : c * EPV + i];
+  for (int i = 0; i < EPV; ++i) {
+    const int k = STYLE == 0 ? (i < EPV / 2 ? c * (EPV / 2) + i
+                                            : (c + half_vecs) * (EPV / 2) + i - EPV / 2)
+                             : c * EPV + i;
+    const float2 a = ang[k];
     cs[i] = a.x;
     sn[i] = a.y;
   }
@@ -130,15 +135,20 @@ __global__ void __launch_bounds__(256)
     const int b = r / H, h = r % H;
     uint4* dst = reinterpret_cast<uint4*>(y + row_offset(out_layout, b, s, h, S, H) * row_elems);
     if (STYLE == 0) {
-      float f[EPV];
-      unpack16(v0, f, T());
+      float f0[EPV], f1[EPV];
+      unpack16(v0, f0, T());
+      unpack16(v1, f1, T());
 #pragma unroll
       for (int i = 0; i < EPV / 2; ++i) {
-        const float a = f[2 * i], bb = f[2 * i + 1];
-        f[2 * i] = a * cs[i] - bb * sn[i];
-        f[2 * i + 1] = a * sn[i] + bb * cs[i];
+        const float a = f0[2 * i], bb = f0[2 * i + 1];
+        f0[2 * i] = a * cs[i] - bb * sn[i];
+        f0[2 * i + 1] = a * sn[i] + bb * cs[i];
+        const float a1 = f1[2 * i], b1 = f1[2 * i + 1];
+        f1[2 * i] = a1 * cs[EPV / 2 + i] - b1 * sn[EPV / 2 + i];
+        f1[2 * i + 1] = a1 * sn[EPV / 2 + i] + b1 * cs[EPV / 2 + i];
       }
-      __stcs(dst + c, pack16(f, T()));
+      __stcs(dst + c, pack16(f0, T()));
+      __stcs(dst + c + half_vecs, pack16(f1, T()));
     } else {
       float f0[EPV], f1[EPV];
       unpack16(v0, f0, T());
@@ -162,7 +172,7 @@ __global__ void __launch_bounds__(256)
   for (int r = row_lo + r0 + kPre * rows_per_pass; r < row_hi; r += rows_per_pass) {
     const uint4* sp = src_of(r);
     const uint4 v0 = __ldcs(sp + c);
-    const uint4 v1 = STYLE == 1 ? __ldcs(sp + c + half_vecs) : v0;
+    const uint4 v1 = __ldcs(sp + c + half_vecs);
     rotate_store(r, v0, v1);
   }
 }

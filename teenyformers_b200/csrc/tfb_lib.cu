@@ -554,7 +554,7 @@ int launch_rope(const T* x, T* y, int B, int S, int H, int D, float ln_base, int
   if (!is_aligned(x, 16) || !is_aligned(y, 16)) return TF_ERR_MISALIGNED;
   const long long rows = (long long)B * H;
   if (!fits_i32(rows) || !fits_i32(rows * S) || S > 0x7fffffff) return TF_ERR_TOO_LARGE;
-  const int cpr = style == TF_ROPE_INTERLEAVED ? D / EPV : D / (2 * EPV);
+  const int cpr = D / (2 * EPV);  // threads per row (two vectors each)
   if (cpr > 256) return TF_ERR_UNSUPPORTED;
   const int rows_per_pass = 256 / cpr;
   // Enough CTAs to fill the GPU: split the (b, h) rows of a position only
