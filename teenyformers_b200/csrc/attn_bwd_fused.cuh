@@ -7,9 +7,10 @@
 //   S^T_j  = K Q_j^T                 (SS, M=128 keys, N=128 queries)
 //   dP^T_j = V dO_j^T                (SS)
 //   dV    += P^T_j dO_j              (A = bf16 P^T packed over S^T in TMEM)
-//   dK    += dS^T_j Q_j              (A = bf16 dS^T packed over dP^T in TMEM)
 //   dQ_j   = dS_j K                  (SS, A = dS from shared memory, M=128
 //                                     queries; result in the dP^T columns)
+//   dK    += dS^T_j Q_j              (SS, A = the same shared tile read as
+//                                     dS^T, K-major)
 // dQ_j leaves through a dedicated warpgroup: TMEM -> registers (which frees
 // the columns for dP^T_{j+1}) -> shared memory -> TMA tensor reduce-add
 // (fp32) into a [BHq, Sq_pad, D] accumulator in the workspace.  A small
@@ -17,10 +18,12 @@
 // the dQ sum order across key tiles is not fixed (fp32 adds in L2).
 //
 // MMA issue order per iteration j (tcgen05 MMAs of one thread run in order):
-//   S^T_{j+1} | [dS_j] dK_j, dQ_j | [dQ_j read out] dP^T_{j+1} | [P_{j+1}] dV_{j+1}
-// so the exponentials of tile j+1 run under dK_j, dQ_j and dP^T_{j+1}.
+//   S^T_{j+1} | [dS_j] dQ_j, dK_j | [dQ_j read out] dP^T_{j+1} | [P_{j+1}] dV_{j+1}
+// so the exponentials of tile j+1 run under dQ_j, dK_j and dP^T_{j+1}.  dQ_j
+// goes before dK_j because the chain dS_j -> dQ_j -> read-out -> dP^T_{j+1}
+// -> dS_{j+1} sets the pace; dK_j only accumulates.
 //
-// TMEM (512 columns): S^T/P^T [0,128), dP^T/dS^T/dQ [128,256),
+// TMEM (512 columns): S^T/P^T [0,128), dP^T/dQ [128,256),
 //                     dV [256,256+D), dK [256+D,256+2D).
 // Warps: 0-3 dQ reduction, 4-11 elementwise (two warpgroups, 64 query
 // columns each; one TMEM lane = one key row per thread), 12 MMA issuer,
@@ -98,15 +101,15 @@ struct BwdFusedCfg {
 
 enum BwdFusedBar {
   FB2_KVFULL = 0, FB2_KVEMPTY = 1, FB2_QFULL = 2, FB2_QEMPTY = 4, FB2_DOFULL = 6,
-  FB2_DOEMPTY = 7, FB2_SFULL = 8, FB2_PFULL = 9, FB2_DPFULL = 10, FB2_DSFULL = 11,
+  FB2_DOEMPTY = 7, FB2_SFULL = 8, FB2_PFULL = 9, FB2_DPFULL = 10, FB2_DSSMEM = 11,
   FB2_DQFULL = 12, FB2_DQEMPTY = 13, FB2_ACC = 14, FB2_ACCFREE = 15, FB2_ITEMFULL = 16,
-  FB2_ITEMEMPTY = 20, FB2_DRAIN = 24, FB2_DSSMEM = 25, FB2_COUNT = 26
+  FB2_ITEMEMPTY = 20, FB2_DRAIN = 24, FB2_COUNT = 25
 };
 constexpr int kItemRing = 4;      // work items the TMA warp may fetch ahead
 constexpr int kItemConsumers = 13;  // MMA warp + 8 elementwise warps + 4 reduction warps
 
-// TMEM column (relative to the operand's base) of the bf16-packed P^T / dS^T
-// for the 16-query K step kk: elementwise warpgroup e packs its 64 query
+// TMEM column (relative to the operand's base) of the bf16-packed P^T for
+// the 16-query K step kk: elementwise warpgroup e packs its 64 query
 // columns [64e, 64e+64) into their first 32 columns, 8 per 16 queries.
 __device__ __forceinline__ constexpr uint32_t packed_col64(int kk) {
   return uint32_t((kk >> 2) * 64 + (kk & 3) * 8);
@@ -180,8 +183,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     mbar_init(bar(FB2_SFULL), 1);
     mbar_init(bar(FB2_PFULL), 8);  // one arrival per elementwise warp
     mbar_init(bar(FB2_DPFULL), 1);
-    mbar_init(bar(FB2_DSFULL), 8);   // dS^T packed in TMEM (dK's A operand)
-    mbar_init(bar(FB2_DSSMEM), 8);   // dS tile in shared memory (dQ's A operand)
+    mbar_init(bar(FB2_DSSMEM), 8);   // dS tile in shared memory (A of dQ and dK)
     mbar_init(bar(FB2_DQFULL), 1);
     mbar_init(bar(FB2_DQEMPTY), 4);  // one per reduction warp
     mbar_init(bar(FB2_ACC), 1);
@@ -328,6 +330,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         __syncwarp();
       };
+      // dK += dS^T Q over K = 128 query rows: A = the shared dS^T tile read
+      // K-major (queries contiguous), B = Q MN-major; then commit `done`
+      const uint64_t d_ds = kmajor_base<C::HALF_BYTES>(sbase + C::OFF_DS);
+      auto issue_dk = [&](uint64_t bq, bool acc, int done) {
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ss(tmem + C::TM_DK, desc_adv(d_ds, kstep_off(kk, C::HALF_BYTES)),
+                   desc_adv(bq, kk * 16 * 128), idesc_acc, (acc || kk > 0) ? 1u : 0u);
+          tc_commit(bar(done));
+        }
+        __syncwarp();
+      };
       // dQ = dS K over K = 128 keys (A, B MN-major), into the dP^T columns
       auto issue_dq = [&]() {
         if (elect_one()) {
@@ -377,15 +392,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             tc_fence_after();
             issue_t(tmem + C::TM_ST, d_k, qdesc(g + 1), FB2_SFULL);
           }
-          ok = mbar_wait_warp(bar(FB2_DSFULL), g & 1, abort_flag, 618);
+          ok = mbar_wait_warp(bar(FB2_DSSMEM), g & 1, abort_flag, 618);
           if (!ok) break;
           tc_fence_after();
-          issue_acc(tmem + C::TM_DK, tmem + C::TM_DPT,
-                    desc_adv(m_q0, (g & 1) * C::TILE_BYTES), it > 0, FB2_QEMPTY + (g & 1));
-          ok = mbar_wait_warp(bar(FB2_DSSMEM), g & 1, abort_flag, 625);
-          if (!ok) break;
-          tc_fence_after();
+          // dQ first: it is on the dependency chain (its read-out frees the
+          // columns of dP^T_{g+1}); dK only accumulates
           issue_dq();
+          issue_dk(desc_adv(m_q0, (g & 1) * C::TILE_BYTES), it > 0, FB2_QEMPTY + (g & 1));
           if (!more) {
             if (elect_one()) {
               tc_commit(bar(FB2_KVEMPTY));  // S^T, dP^T, dQ of this item are all issued
@@ -420,8 +433,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const uint32_t lane_base = uint32_t(wq * 32) << 16;
     const float sl2 = p.scale_log2;
     const int col0 = ewg * 64;
-    // dS^T row `row` in the MN-major SW128 tile read by the dQ MMA: half ewg,
-    // 16-byte chunk c of the row at physical chunk c ^ (row & 7)
+    // dS^T row `row` in the SW128 tile read by the dQ MMA (MN-major) and the
+    // dK MMA (K-major): half ewg, 16-byte chunk c of the row at physical chunk
+    // c ^ (row & 7)
     const uint32_t ds_row = sbase + C::OFF_DS + ewg * C::HALF_BYTES + row * 128;
     const bool epi_issuer = (warp & 3) == 0 && lane == 0;  // first thread of the warpgroup
     bool ok = true;
@@ -496,8 +510,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive_warp(bar(FB2_PFULL));
-        // Phase 2: dS^T = P^T (dP^T - D): bf16 packed over dP^T (A of dK) and
-        // into the shared dS tile (A of dQ).
+        // Phase 2: dS^T = P^T (dP^T - D), bf16 into the shared dS tile (A of
+        // dQ and dK).
         ok = __all_sync(0xffffffffu, mbar_wait(bar(FB2_DPFULL), g & 1, abort_flag, 633));
         if (!ok) break;
         tc_fence_after();
@@ -521,17 +535,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             dk[2 * v4] = pack_bf16x2(dsv[0], dsv[1]);
             dk[2 * v4 + 1] = pack_bf16x2(dsv[2], dsv[3]);
           }
-          tmem_st8(tmem + lane_base + C::TM_DPT + col0 + sub * 8, dk);
           const uint32_t ch = uint32_t(2 * sub);
           st_shared_v4(ds_row + ((ch ^ uint32_t(row & 7)) << 4), dk[0], dk[1], dk[2], dk[3]);
           st_shared_v4(ds_row + (((ch + 1) ^ uint32_t(row & 7)) << 4), dk[4], dk[5], dk[6],
                        dk[7]);
         }
-        // dK reads dS^T from TMEM: released before the shared-memory proxy fence
-        // that only the dQ MMA (dS from the shared tile) needs
-        tmem_wait_st();
+        // dQ and dK read the shared tile; dQ overwrites the dP^T columns read
+        // above (tcgen05.wait::ld done), hence the tcgen05 fence as well
         tc_fence_before();
-        mbar_arrive_warp(bar(FB2_DSFULL));
         fence_proxy_async_smem();
         mbar_arrive_warp(bar(FB2_DSSMEM));
       }
