@@ -21,9 +21,10 @@
 //   S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
 // P_t (bf16 pairs) overwrites the first 64 columns of S_t; the next S_t MMA
 // is issued after the P_t V_j MMA, and tcgen05 MMAs of one thread execute in
-// issue order.  P_t is handed to the MMA issuer in two 64-key halves (two
-// phases of one mbarrier per iteration) so the first half of P_t V_j runs
-// while the softmax finishes the second half.  The issuing thread blocks
+// issue order.  P_t is handed to the MMA issuer once, whole: handing it over
+// in two 64-key halves (the first half of P_t V_j under the second half of
+// the softmax) measured ~1 % slower, the extra hand-off costing the single
+// issuing warp more than the overlap gained.  The issuing thread blocks
 // while the tensor pipe's queue is full, so its bookkeeping (slot-release
 // commits) is deferred until the next batch of MMAs is queued.  The running
 // max is rescaled lazily: O and l are only rescaled when the row max grows
@@ -74,13 +75,12 @@ enum FwdBar {
   FB_VFULL = 5,   // 2
   FB_VEMPTY = 7,  // 2
   FB_SFULL = 9,   // 2
-  FB_PFULL = 11,  // 2: keys 0..63 of P_t ready
+  FB_PFULL = 11,  // 2: P_t ready in TMEM
   FB_ODONE = 13,  // 2
   FB_DRAIN = 15,
-  FB_PFULL1 = 16,  // 2: keys 64..127 of P_t ready
-  FB_QEMPTY = 18,  // every S MMA of the item is done: Q may be replaced
-  FB_OFREE = 19,   // 2: the epilogue has read O_t out of TMEM
-  FB_COUNT = 21
+  FB_QEMPTY = 16,  // every S MMA of the item is done: Q may be replaced
+  FB_OFREE = 17,   // 2: the epilogue has read O_t out of TMEM
+  FB_COUNT = 19
 };
 
 // Waits without looking at the abort flag (used to drain in-flight async
@@ -165,7 +165,6 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(FB_VEMPTY + s), 1);
       mbar_init(bar(FB_SFULL + s), 1);
       mbar_init(bar(FB_PFULL + s), 4);  // one arrival per softmax warp
-      mbar_init(bar(FB_PFULL1 + s), 4);
       mbar_init(bar(FB_ODONE + s), 1);
       mbar_init(bar(FB_OFREE + s), 4);
     }
@@ -325,15 +324,12 @@ __global__ void __launch_bounds__(320, 1)
             if (!ok) break;
           }
           const uint32_t ph = uint32_t(st_[t] + j) & 1u;
-          ok = mbar_wait_warp(bar(FB_PFULL + t), ph, abort_flag, 204);  // keys 0..63 of P_t
+          ok = mbar_wait_warp(bar(FB_PFULL + t), ph, abort_flag, 204);
           if (!ok) break;
           tc_fence_after();
           issue_pv_half(t, s, 0, j > 0, pend_v >= 0 ? FB_VEMPTY + pend_v : -1,
                         pend_k >= 0 ? FB_KEMPTY + pend_k : -1);
           pend_v = pend_k = -1;
-          ok = mbar_wait_warp(bar(FB_PFULL1 + t), ph, abort_flag, 207);  // keys 64..127
-          if (!ok) break;
-          tc_fence_after();
           const bool more = j + 1 < nkv(t);
           issue_pv_half(t, s, 1, true, more ? -1 : FB_ODONE + t, -1);
           if (more) {
@@ -427,7 +423,7 @@ __global__ void __launch_bounds__(320, 1)
         const uint64_t nbx2 = f2_make(-base, -base);
         uint64_t acc2[2] = {f2_make(0.0f, 0.0f), f2_make(0.0f, 0.0f)};
         // P = 2^(s*scale*log2e - m) in bf16, written over the S columns already
-        // read, 32 keys per store; handed off per 64-key half.
+        // read, 32 keys per store; handed to the MMA warp once complete.
   #pragma unroll
         for (int half = 0; half < 2; ++half) {
   #pragma unroll
@@ -459,10 +455,10 @@ __global__ void __launch_bounds__(320, 1)
               tmem_st32(tO + c * 32, orow);
             }
           }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive_warp(bar((half == 0 ? FB_PFULL : FB_PFULL1) + t));
         }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive_warp(bar(FB_PFULL + t));
         float a0, a1, a2, a3;
         f2_split(acc2[0], a0, a1);
         f2_split(acc2[1], a2, a3);
