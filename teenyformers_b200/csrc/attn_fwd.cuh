@@ -23,7 +23,7 @@
 // is issued after the P_t V_j MMA, and tcgen05 MMAs of one thread execute in
 // issue order.  P_t is handed to the MMA issuer once, whole: handing it over
 // in two 64-key halves (the first half of P_t V_j under the second half of
-// the softmax) measured ~1 % slower, the extra hand-off costing the single
+// the softmax) measured ~1.5 % slower, the extra hand-off costing the single
 // issuing warp more than the overlap gained.  The issuing thread blocks
 // while the tensor pipe's queue is full, so its bookkeeping (slot-release
 // commits) is deferred until the next batch of MMAs is queued.  The running
