@@ -516,6 +516,12 @@ def main():
     status = tfb.device_status(clear=True)
 
     # ---- RoPE + transpose leg (config #2, every rank runs the full config) ----
+    # The tensor-bound steps above leave the GPU at its power cap with lowered
+    # SM clocks, which stretch the fixed per-launch work of a ~24 us kernel; the
+    # memory-bound legs start after a second of idle, by which the clocks recover.
+    if not (args.no_rope and args.no_decode):
+        torch.cuda.synchronize()
+        time.sleep(1.0)
     rope = None
     if not args.no_rope:
         rb, rs, rh, rd = CFG2["batch"], CFG2["seq"], CFG2["heads"], CFG2["head_dim"]
@@ -565,7 +571,8 @@ def main():
                                          "rope.rs pairing"},
                 "workload": "config#2 x[4,2048,32,128] bf16 -> RoPE(rotate-half, theta 1e4) -> "
                             "[4,32,2048,128]; 4 rotating buffer sets (512 MiB) so reads miss L2; "
-                            f"{n_rope} launches in one CUDA graph replay per style"}
+                            f"{n_rope} launches in one CUDA graph replay per style, after 1 s "
+                            "idle (clocks recover from the power cap of the fwd+bwd steps)"}
         del xs, ys
 
     # the memory-bound decode leg goes before the long tensor-bound legs, which leave the
