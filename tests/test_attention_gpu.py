@@ -43,6 +43,8 @@ CASES = [
     (1, 3, 1, 130, 300, 128, False),    # cross attention Nq < Nk, GQA 3:1
     (1, 1, 1, 1, 1, 128, True),         # S = 1
     (1, 2, 2, 640, 640, 128, True),     # several query-tile pairs
+    (2, 4, 1, 512, 512, 64, False),     # D=64, GQA 4:1, several key tiles per head
+    (1, 2, 2, 1000, 1000, 64, True),    # D=64, ragged, several query-tile pairs
 ]
 
 
