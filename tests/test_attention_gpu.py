@@ -45,6 +45,8 @@ CASES = [
     (1, 2, 2, 640, 640, 128, True),     # several query-tile pairs
     (2, 4, 1, 512, 512, 64, False),     # D=64, GQA 4:1, several key tiles per head
     (1, 2, 2, 1000, 1000, 64, True),    # D=64, ragged, several query-tile pairs
+    (1, 8, 1, 384, 384, 128, False),    # GQA 8:1 (config #4's ratio): dK/dV over 8 query heads
+    (2, 16, 2, 256, 320, 64, False),    # GQA 8:1, D=64, Sq != Sk, KV heads of two batches
 ]
 
 
